@@ -1,0 +1,106 @@
+/*
+ * tiledattention_b200 — C ABI of the B200 (sm_100a) scaled-dot-product-attention
+ * forward operator.
+ *
+ * This is the native boundary of the package: plain pointers, sizes and a raw
+ * CUDA stream handle, no torch types. Every entry point returns a status code
+ * (TA_OK or one of the TA_ERR_* values below) and never throws across the ABI.
+ *
+ * Reference interfaces replaced (paths relative to thisistaimur/TiledAttention):
+ *   - src/tiledattention/kernels/flash_fwd.py:821-973  run_flash_fwd(q, k, v, *, causal, scale)
+ *       host launcher: reshape to [B*H,S,D], K transpose view, out = empty_like(q),
+ *       variant/tile policy, grid (B*H, ceil(S/TM)).
+ *   - src/tiledattention/kernels/flash_fwd.py:786-818  _launch_cutile_kernel(...)
+ *       launch on the caller's stream with an optional sync mode.
+ *   - src/tiledattention/kernels/flash_fwd.py:301-783  the cuTile kernel bodies
+ *       (direct / aligned / chunked, fp16 or fp32 accumulation).
+ *   - src/tiledattention/kernels/compile_cache.py:10-37 JIT kernel cache (replaced by
+ *       ahead-of-time sm_100a variants specialised per head dim, dtype and causal flag).
+ *   - torch-ext/torch_binding.cpp:6-19 / tiledattention_cuda/tiledattention.cu:13-33
+ *       the native op slot of the Hugging Face kernel-builder build.
+ *
+ * Layout: q, k, v, o are 4-D [B, H, S, D] tensors given by a base pointer and four
+ * element strides (batch, head, sequence, dim). The dim stride must be 1; the other
+ * strides times the element size must be multiples of 16 bytes and the base pointers
+ * 16-byte aligned (TMA descriptor rules). Supported head dims: 64, 128.
+ */
+#ifndef TILEDATTENTION_B200_H
+#define TILEDATTENTION_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define TA_OK                   0
+#define TA_ERR_INVALID_ARGUMENT 1  /* null pointer, non-positive size, bad scale      */
+#define TA_ERR_UNSUPPORTED_DIM  2  /* head dim not in {64, 128}                       */
+#define TA_ERR_UNSUPPORTED_DTYPE 3 /* dtype not TA_DTYPE_F16 / TA_DTYPE_BF16          */
+#define TA_ERR_LAYOUT           4  /* stride / alignment not expressible as a TMA map */
+#define TA_ERR_CUDA             5  /* a CUDA runtime call failed (see ta_last_error)  */
+#define TA_ERR_DRIVER           6  /* driver entry point / tensor-map encode failure  */
+#define TA_ERR_DEVICE           7  /* current device is not compute capability 10.0   */
+
+/* Element types (match the reference's accepted dtypes, checks.py:50-55). */
+#define TA_DTYPE_F16  0
+#define TA_DTYPE_BF16 1
+
+/* Device status word bits, written by the kernel with atomicOr when a bounded wait
+ * inside the kernel expires (the kernel then drains its in-flight copies and MMAs,
+ * frees its tensor memory and returns instead of hanging). */
+#define TA_DEVSTAT_TIMEOUT_LOAD    1u
+#define TA_DEVSTAT_TIMEOUT_MMA     2u
+#define TA_DEVSTAT_TIMEOUT_SOFTMAX 4u
+#define TA_DEVSTAT_TIMEOUT_EPILOG  8u
+#define TA_DEVSTAT_TIMEOUT_DRAIN   16u
+
+/*
+ * ta_sdpa_fwd — o = softmax(q k^T * scale + mask) v, one launch, asynchronous on `stream`.
+ *
+ * Replaces run_flash_fwd (flash_fwd.py:821-973) + _launch_cutile_kernel (:786-818).
+ * Mask semantics follow flash_fwd.py:400-423: key index < S, and for causal=1 the
+ * top-left causal rule row >= col (S_q == S_kv, checks.py:45-46).
+ *
+ *   q, k, v       device pointers, dtype `dtype`, [B,H,S,D] with the given strides
+ *   o             device pointer for the output, same dtype, [B,H,S,D] with o_strides
+ *   lse           optional device float32 [B*H*S] (row-major over (b,h,s)); receives the
+ *                 natural-log log-sum-exp of the scaled, masked scores per query row.
+ *                 Pass NULL to skip (the reference has no lse output).
+ *   *_strides     4 element strides each: batch, head, seq, dim (dim stride must be 1)
+ *   scale         positive softmax scale (the Python API resolves the default 1/sqrt(D),
+ *                 sdpa.py:46-47)
+ *   dev_status    optional device uint32 word; the kernel ORs TA_DEVSTAT_* bits into it
+ *   stream        cudaStream_t of the caller (torch's current stream in the binding)
+ *
+ * Allocates nothing. Returns TA_OK once the launch is enqueued.
+ */
+int ta_sdpa_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
+                int B, int H, int S, int D,
+                const int64_t* q_strides, const int64_t* k_strides,
+                const int64_t* v_strides, const int64_t* o_strides,
+                int dtype, int causal, float scale,
+                unsigned int* dev_status, void* stream);
+
+/*
+ * ta_device_supported — 1 if `device` is a compute-capability 10.0 GPU this build runs
+ * on, 0 otherwise. Replaces the runtime gate require_supported_runtime
+ * (src/tiledattention/_runtime.py:161-191), narrowed to the sm_100a build.
+ */
+int ta_device_supported(int device);
+
+/* ta_status_string — static text for a TA_* status code. */
+const char* ta_status_string(int status);
+
+/* ta_last_error — text of the last failure on the calling host thread ("" if none). */
+const char* ta_last_error(void);
+
+/* ta_abi_version — ABI version of this library (major*100 + minor). */
+int ta_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TILEDATTENTION_B200_H */

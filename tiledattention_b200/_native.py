@@ -1,0 +1,104 @@
+"""ctypes binding of the C ABI declared in include/tiledattention_b200.h.
+
+The shared library is built ahead of time for sm_100a (tiledattention_b200/build.py)
+and lives in-tree at tiledattention_b200/_lib/libtiledattention_b200.so. There is no
+fallback: if the library is missing, loading raises DependencyError.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+from ._errors import DependencyError
+
+LIB_NAME = "libtiledattention_b200.so"
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", LIB_NAME)
+
+# Status codes (include/tiledattention_b200.h).
+TA_OK = 0
+TA_ERR_INVALID_ARGUMENT = 1
+TA_ERR_UNSUPPORTED_DIM = 2
+TA_ERR_UNSUPPORTED_DTYPE = 3
+TA_ERR_LAYOUT = 4
+TA_ERR_CUDA = 5
+TA_ERR_DRIVER = 6
+TA_ERR_DEVICE = 7
+
+TA_DTYPE_F16 = 0
+TA_DTYPE_BF16 = 1
+
+DEVSTAT_BITS = {
+    1: "TMA producer wait timed out",
+    2: "MMA issuer wait timed out",
+    4: "softmax wait timed out",
+    8: "epilogue wait timed out",
+    16: "drain of in-flight copies/MMAs timed out",
+}
+
+# Every symbol include/tiledattention_b200.h declares, with its ctypes signature.
+_I64P = ctypes.POINTER(ctypes.c_int64)
+SIGNATURES = {
+    "ta_sdpa_fwd": (
+        ctypes.c_int,
+        [
+            ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+            ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+            _I64P, _I64P, _I64P, _I64P,
+            ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p,
+        ],
+    ),
+    "ta_device_supported": (ctypes.c_int, [ctypes.c_int]),
+    "ta_status_string": (ctypes.c_char_p, [ctypes.c_int]),
+    "ta_last_error": (ctypes.c_char_p, []),
+    "ta_abi_version": (ctypes.c_int, []),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+def load_library(path: str | None = None) -> ctypes.CDLL:
+    """Load (once) and return the native library with its signatures applied."""
+    global _lib
+    with _lock:
+        if _lib is not None and path is None:
+            return _lib
+        lib_path = path or LIB_PATH
+        if not os.path.exists(lib_path):
+            raise DependencyError(
+                f"native library {lib_path} not found; build it with "
+                "`python -m tiledattention_b200.build`."
+            )
+        try:
+            lib = ctypes.CDLL(lib_path)
+        except OSError as exc:
+            raise DependencyError(f"cannot load {lib_path}: {exc}") from exc
+        for name, (restype, argtypes) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = restype
+            fn.argtypes = argtypes
+        if path is None:
+            _lib = lib
+        return lib
+
+
+def last_error(lib: ctypes.CDLL) -> str:
+    msg = lib.ta_last_error()
+    return msg.decode() if msg else ""
+
+
+def status_string(lib: ctypes.CDLL, code: int) -> str:
+    msg = lib.ta_status_string(code)
+    return msg.decode() if msg else ""
+
+
+def strides4(strides) -> ctypes.Array:
+    arr = (ctypes.c_int64 * 4)(*[int(s) for s in strides])
+    return arr
+
+
+def describe_devstat(word: int) -> str:
+    parts = [text for bit, text in DEVSTAT_BITS.items() if word & bit]
+    return "; ".join(parts) if parts else f"status 0x{word:x}"

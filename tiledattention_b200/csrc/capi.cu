@@ -1,0 +1,185 @@
+// C ABI of tiledattention_b200: argument checks, TMA tensor-map encoding and the
+// launch of the sm_100a SDPA forward kernel on the caller's stream.
+//
+// Replaces the reference host launcher run_flash_fwd
+// (src/tiledattention/kernels/flash_fwd.py:821-973) and _launch_cutile_kernel
+// (flash_fwd.py:786-818). The reference reshapes to [B*H,S,D] with .contiguous()
+// and builds a K transpose view; here each operand is described by a 4-D TMA map
+// (D, S, H, B) over the caller's own strides, so no copy or transpose is made.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "sdpa_fwd_sm100.h"
+#include "tiledattention_b200.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 4-D map over a [B,H,S,D] operand: dims (D, S, H, B), box 64 x 128 x 1 x 1,
+// 128-byte swizzle, zero fill out of bounds (ragged sequence tail).
+int make_map(CUtensorMap* map, const void* base, int B, int H, int S, int D,
+             const int64_t* st, int dtype, const char* name) {
+  auto enc = encode_fn();
+  if (!enc) return fail(TA_ERR_DRIVER, "cuTensorMapEncodeTiled entry point unavailable");
+  const uint64_t esz = 2;
+  if (st[3] != 1) return fail(TA_ERR_LAYOUT, "%s: head-dim stride must be 1 (got %lld)", name,
+                              static_cast<long long>(st[3]));
+  if (reinterpret_cast<uintptr_t>(base) % 16)
+    return fail(TA_ERR_LAYOUT, "%s: base pointer not 16-byte aligned", name);
+  const int64_t ext[3] = {S, H, B};
+  const int64_t str[3] = {st[2], st[1], st[0]};
+  cuuint64_t gdim[4] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(S),
+                        static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(B)};
+  cuuint64_t gstride[3];
+  // A unit dimension's stride is never used to form an address; give it a legal value.
+  uint64_t span = static_cast<uint64_t>(D) * esz;
+  for (int i = 0; i < 3; ++i) {
+    uint64_t s = static_cast<uint64_t>(str[i]) * esz;
+    if (ext[i] == 1 || str[i] <= 0) {
+      if (ext[i] != 1) return fail(TA_ERR_LAYOUT, "%s: non-positive stride", name);
+      s = (span + 15) / 16 * 16;
+    }
+    if (s % 16) return fail(TA_ERR_LAYOUT, "%s: stride %d not a multiple of 16 bytes", name, i);
+    gstride[i] = s;
+    span = s * static_cast<uint64_t>(ext[i]);
+  }
+  cuuint32_t box[4] = {64, 128, 1, 1};
+  cuuint32_t estride[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, dtype == TA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                               : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                   4, const_cast<void*>(base), gdim, gstride, box, estride,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(TA_ERR_LAYOUT, "%s: cuTensorMapEncodeTiled rejected the layout (CUresult %d)",
+                name, static_cast<int>(r));
+  return TA_OK;
+}
+
+int check_device() {
+  static int cached[64];  // 0 unknown, 1 ok, 2 unsupported
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail(TA_ERR_CUDA, "cudaGetDevice failed");
+  if (dev < 64 && cached[dev] == 1) return TA_OK;
+  if (!ta_device_supported(dev))
+    return fail(TA_ERR_DEVICE, "device %d is not a compute-capability 10.0 (B200) GPU", dev);
+  if (dev < 64) cached[dev] = 1;
+  return TA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ta_abi_version(void) { return 100; }
+
+const char* ta_last_error(void) { return g_last_error.c_str(); }
+
+const char* ta_status_string(int status) {
+  switch (status) {
+    case TA_OK: return "ok";
+    case TA_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case TA_ERR_UNSUPPORTED_DIM: return "unsupported head dim (supported: 64, 128)";
+    case TA_ERR_UNSUPPORTED_DTYPE: return "unsupported dtype (supported: float16, bfloat16)";
+    case TA_ERR_LAYOUT: return "layout not expressible as a TMA tensor map";
+    case TA_ERR_CUDA: return "CUDA runtime error";
+    case TA_ERR_DRIVER: return "CUDA driver entry point error";
+    case TA_ERR_DEVICE: return "unsupported device (requires compute capability 10.0)";
+    default: return "unknown status";
+  }
+}
+
+int ta_device_supported(int device) {
+  int major = 0, minor = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device) != cudaSuccess)
+    return 0;
+  if (cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device) != cudaSuccess)
+    return 0;
+  return (major == 10 && minor == 0) ? 1 : 0;
+}
+
+int ta_sdpa_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int B, int H,
+                int S, int D, const int64_t* q_strides, const int64_t* k_strides,
+                const int64_t* v_strides, const int64_t* o_strides, int dtype, int causal,
+                float scale, unsigned int* dev_status, void* stream) {
+  g_last_error.clear();
+  if (!q || !k || !v || !o || !q_strides || !k_strides || !v_strides || !o_strides)
+    return fail(TA_ERR_INVALID_ARGUMENT, "null pointer argument");
+  if (B <= 0 || H <= 0 || S <= 0)
+    return fail(TA_ERR_INVALID_ARGUMENT, "B, H, S must be positive (got %d, %d, %d)", B, H, S);
+  if (D != 64 && D != 128) return fail(TA_ERR_UNSUPPORTED_DIM, "head dim %d not in {64, 128}", D);
+  if (dtype != TA_DTYPE_F16 && dtype != TA_DTYPE_BF16)
+    return fail(TA_ERR_UNSUPPORTED_DTYPE, "dtype code %d", dtype);
+  if (!(scale > 0.f) || !std::isfinite(scale))
+    return fail(TA_ERR_INVALID_ARGUMENT, "scale must be a positive finite number");
+  if (o_strides[3] != 1) return fail(TA_ERR_LAYOUT, "o: head-dim stride must be 1");
+  if (reinterpret_cast<uintptr_t>(o) % 16 || (o_strides[2] * 2) % 16 || (o_strides[1] * 2) % 16 ||
+      (o_strides[0] * 2) % 16)
+    return fail(TA_ERR_LAYOUT, "o: base / strides must be 16-byte aligned");
+  if (static_cast<int64_t>(B) * H > (1ll << 24))
+    return fail(TA_ERR_INVALID_ARGUMENT, "B*H too large");
+  int rc = check_device();
+  if (rc) return rc;
+
+  CUtensorMap mq, mk, mv;
+  if ((rc = make_map(&mq, q, B, H, S, D, q_strides, dtype, "q"))) return rc;
+  if ((rc = make_map(&mk, k, B, H, S, D, k_strides, dtype, "k"))) return rc;
+  if ((rc = make_map(&mv, v, B, H, S, D, v_strides, dtype, "v"))) return rc;
+
+  ta::FwdParams p{};
+  p.o = o;
+  p.lse = lse;
+  p.status = dev_status;
+  p.o_sb = o_strides[0];
+  p.o_sh = o_strides[1];
+  p.o_ss = o_strides[2];
+  p.S = S;
+  p.H = H;
+  p.BH = B * H;
+  p.n_qblk = (S + ta::rows_per_cta() - 1) / ta::rows_per_cta();
+  p.scale_log2 = static_cast<float>(static_cast<double>(scale) * 1.4426950408889634);
+  if (static_cast<int64_t>(p.BH) * p.n_qblk > 0x7fffffffll)
+    return fail(TA_ERR_INVALID_ARGUMENT, "grid too large");
+
+  cudaError_t err = ta::launch_sdpa_fwd(mq, mk, mv, p, D, dtype == TA_DTYPE_BF16, causal != 0,
+                                        static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess)
+    return fail(TA_ERR_CUDA, "kernel launch failed: %s", cudaGetErrorString(err));
+  return TA_OK;
+}
+
+}  // extern "C"

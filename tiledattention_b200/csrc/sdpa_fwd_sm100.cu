@@ -1,0 +1,469 @@
+// SDPA forward for B200 (sm_100a): TMA + mbarrier pipeline, tcgen05 MMAs with
+// accumulators in tensor memory, warp-specialised online softmax.
+//
+// Algorithm (same maths as the reference cuTile kernel,
+// src/tiledattention/kernels/flash_fwd.py:374-446 of thisistaimur/TiledAttention):
+//   for each query row r:  m = -inf, l = 0, acc = 0
+//   for each key tile:     s = q_r . k_c * scale, masked to -inf where c >= S or
+//                          (causal and c > r)                    (flash_fwd.py:400-423)
+//                          m' = max(m, max_c s); alpha = exp(m - m')
+//                          p = exp(s - m'); l = l*alpha + sum p; acc = acc*alpha + p v
+//   o_r = acc / l                                               (flash_fwd.py:438-444)
+// Differences in precision, all towards the fp32 oracle: scores and P.V products are
+// accumulated in fp32 tensor memory (the cuTile kernel rounds each tile product to
+// the input dtype), and the exponent is evaluated as exp2 with log2(e) folded into
+// the scale. The running max is rescaled lazily: the accumulator is only rescaled
+// when the max grows by more than 2^8, which is exact after the final division by l.
+//
+// CTA organisation (one CTA per SM: 192 KB shared memory, all 512 TMEM columns):
+//   one CTA = one (batch, head) pair x 256 query rows = two 128-row query tiles
+//   warps 0-3  softmax + epilogue for query tile 0 (thread i owns TMEM lane / row i)
+//   warps 4-7  softmax + epilogue for query tile 1
+//   warp  8    TMA producer: Q tiles once, then K_0, V_0, K_1, V_1 ... through a ring
+//   warp  9    TMEM allocator and single-thread tcgen05.mma issuer
+// Tensor memory: S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [256+D,256+2D) columns;
+// P_t (16-bit, two per column) overwrites the first 64 columns of S_t and feeds the
+// P.V MMA straight from tensor memory.
+// MMA issue order per key tile j (in-order tensor pipe):
+//   PV0(j-1)... S0(j) S1(j) | PV0(j) S0(j+1) | PV1(j) S1(j+1) ...
+// so that when S_t(j+1) is signalled complete, PV_t(j) has completed too and
+// the softmax warps may rescale O_t without another barrier.
+//
+// Every wait is bounded (shared abort flag + global-timer timeout); on expiry the
+// kernel records TA_DEVSTAT_* bits in the status word, drains its own in-flight TMA
+// copies and MMAs, frees tensor memory and returns.
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "sm100_ptx.cuh"
+#include "sdpa_fwd_sm100.h"
+#include "tiledattention_b200.h"
+
+namespace ta {
+
+constexpr int kRowsPerTile = 128;  // query rows per tile (= TMEM lanes)
+constexpr int kTilesPerCta = 2;    // query tiles per CTA
+constexpr int kRowsPerCta = kRowsPerTile * kTilesPerCta;
+constexpr int kKeysPerTile = 128;  // keys per K/V tile
+constexpr int kThreads = 320;
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr uint32_t kTmemCols = 512;
+constexpr float kRescaleThreshold = 8.0f;      // log2 units
+constexpr uint64_t kTimeoutNs = 1000000000ull;  // 1 s per wait
+
+template <int D>
+struct Layout {
+  static constexpr int kTileBytes = kRowsPerTile * D * 2;  // 128 rows x D x 16-bit
+  static constexpr int kChunks = D / 64;                   // 128-byte swizzle atoms per row
+  static constexpr int kStages = (D == 64) ? 6 : 4;
+  static constexpr int kQOff = 0;
+  static constexpr int kKVOff = kQOff + kTilesPerCta * kTileBytes;
+  static constexpr int kBarOff = kKVOff + kStages * kTileBytes;
+  static constexpr int kBytes = kBarOff + 256;
+  static constexpr int kDynSmem = kBytes + 1024;  // slack for 1024-byte alignment
+};
+
+struct Barriers {
+  uint64_t q_full;
+  uint64_t s_full[2];
+  uint64_t p_full[2];
+  uint64_t o_final[2];
+  uint64_t drain;
+  uint64_t kv_full[8];
+  uint64_t kv_empty[8];
+  uint32_t tmem_base;
+  int abort_flag;
+};
+static_assert(sizeof(Barriers) <= 256, "barrier block");
+
+__device__ __forceinline__ void report(const FwdParams& p, uint32_t code, volatile int* abort_flag) {
+  *abort_flag = 1;
+  if (p.status) atomicOr(p.status, code);
+}
+
+// Two fp32 values -> one 32-bit word of two 16-bit values, `lo` in the low half.
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  uint32_t r;
+  if constexpr (BF16)
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  else
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+template <bool BF16>
+__device__ __forceinline__ float2 unpack2(uint32_t w) {
+  if constexpr (BF16) {
+    return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+  } else {
+    __half2 h = *reinterpret_cast<__half2*>(&w);
+    return __half22float2(h);
+  }
+}
+
+template <int D, bool BF16, bool CAUSAL>
+__global__ void __launch_bounds__(kThreads, 1)
+    sdpa_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q,
+                    const __grid_constant__ CUtensorMap tmap_k,
+                    const __grid_constant__ CUtensorMap tmap_v, const FwdParams p) {
+  using L = Layout<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* q_smem = smem + L::kQOff;
+  uint8_t* kv_smem = smem + L::kKVOff;
+  Barriers* bars = reinterpret_cast<Barriers*>(smem + L::kBarOff);
+  volatile int* abort_flag = &bars->abort_flag;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // Block -> (bh, query block). Consecutive blocks share a (b,h) so its K/V stays in L2;
+  // inside a (b,h) the longest causal rows are issued first.
+  const int bh = blockIdx.x / p.n_qblk;
+  const int qblk = p.n_qblk - 1 - (blockIdx.x % p.n_qblk);
+  const int b = bh / p.H;
+  const int h = bh % p.H;
+  const int S = p.S;
+  const int q_row0 = qblk * kRowsPerCta;
+  const int kv_rows = CAUSAL ? min(S, q_row0 + kRowsPerCta) : S;
+  const int n_kv = (kv_rows + kKeysPerTile - 1) / kKeysPerTile;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->q_full, 1);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&bars->s_full[t], 1);
+      mbar_init(&bars->p_full[t], kRowsPerTile);
+      mbar_init(&bars->o_final[t], 1);
+    }
+    mbar_init(&bars->drain, 1);
+    for (int s = 0; s < L::kStages; ++s) {
+      mbar_init(&bars->kv_full[s], 1);
+      mbar_init(&bars->kv_empty[s], 1);
+    }
+    bars->abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == kProducerWarp && lane == 0) {
+    prefetch_tmap(&tmap_q);
+    prefetch_tmap(&tmap_k);
+    prefetch_tmap(&tmap_v);
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(&bars->tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+
+  if (warp == kProducerWarp) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&bars->q_full, kTilesPerCta * L::kTileBytes);
+      for (int t = 0; t < kTilesPerCta; ++t)
+        for (int c = 0; c < L::kChunks; ++c)
+          tma_load_4d(q_smem + t * L::kTileBytes + c * (kRowsPerTile * 128), &tmap_q,
+                      &bars->q_full, c * 64, q_row0 + t * kRowsPerTile, h, b);
+      int issued = 0;
+      for (int it = 0; it < 2 * n_kv; ++it) {
+        const int st = it % L::kStages;
+        const uint32_t ph = (it / L::kStages) & 1;
+        if (!mbar_wait_bounded(&bars->kv_empty[st], ph ^ 1, abort_flag, kTimeoutNs)) {
+          if (!*abort_flag) report(p, TA_DEVSTAT_TIMEOUT_LOAD, abort_flag);
+          break;
+        }
+        mbar_arrive_expect_tx(&bars->kv_full[st], L::kTileBytes);
+        const CUtensorMap* map = (it & 1) ? &tmap_v : &tmap_k;
+        const int key0 = (it >> 1) * kKeysPerTile;
+        for (int c = 0; c < L::kChunks; ++c)
+          tma_load_4d(kv_smem + st * L::kTileBytes + c * (kKeysPerTile * 128), map,
+                      &bars->kv_full[st], c * 64, key0, h, b);
+        issued = it + 1;
+      }
+      // Drain: every copy this thread issued must land before the CTA may exit.
+      volatile int no_abort = 0;
+      bool ok = mbar_wait_bounded(&bars->q_full, 0, &no_abort, kTimeoutNs);
+      for (int it = max(0, issued - L::kStages); it < issued; ++it)
+        ok &= mbar_wait_bounded(&bars->kv_full[it % L::kStages], (it / L::kStages) & 1,
+                                &no_abort, kTimeoutNs);
+      if (!ok && p.status) atomicOr(p.status, TA_DEVSTAT_TIMEOUT_DRAIN);
+    }
+    __syncwarp();
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t kIdescQK = idesc_f16(kRowsPerTile, kKeysPerTile, BF16, false, false);
+      constexpr uint32_t kIdescPV = idesc_f16(kRowsPerTile, D, BF16, false, true);
+      const uint32_t q_addr = smem_u32(q_smem);
+      const uint32_t kv_addr = smem_u32(kv_smem);
+      auto issue_qk = [&](int t, int st) {
+        const uint32_t qa = q_addr + t * L::kTileBytes;
+        const uint32_t ka = kv_addr + st * L::kTileBytes;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * (kRowsPerTile * 128) + (kk & 3) * 32;
+          mma_ss(tmem + t * 128, sdesc_sw128(qa + off, 16, 1024), sdesc_sw128(ka + off, 16, 1024),
+                 kIdescQK, kk > 0 ? 1u : 0u);
+        }
+      };
+      auto issue_pv = [&](int t, int st, bool acc) {
+        const uint32_t va = kv_addr + st * L::kTileBytes;
+#pragma unroll
+        for (int kk = 0; kk < kKeysPerTile / 16; ++kk) {
+          mma_ts(tmem + 256 + t * D, tmem + t * 128 + kk * 8,
+                 sdesc_sw128(va + kk * 16 * 128, kKeysPerTile * 128, 1024), kIdescPV,
+                 (acc || kk > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = mbar_wait_bounded(&bars->q_full, 0, abort_flag, kTimeoutNs);
+      int it = 0;
+      if (ok) {
+        const int st = 0;
+        ok = mbar_wait_bounded(&bars->kv_full[st], 0, abort_flag, kTimeoutNs);
+        if (ok) {
+          tc_fence_after();
+          issue_qk(0, st);
+          mma_commit(&bars->s_full[0]);
+          issue_qk(1, st);
+          mma_commit(&bars->s_full[1]);
+          mma_commit(&bars->kv_empty[st]);
+          it = 1;
+        }
+      }
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int st_v = it % L::kStages;
+        ok = mbar_wait_bounded(&bars->kv_full[st_v], (it / L::kStages) & 1, abort_flag, kTimeoutNs);
+        if (!ok) break;
+        ++it;
+        const bool more = (j + 1 < n_kv);
+        const int st_k = it % L::kStages;
+        // query tile 0
+        ok = mbar_wait_bounded(&bars->p_full[0], j & 1, abort_flag, kTimeoutNs);
+        if (!ok) break;
+        tc_fence_after();
+        issue_pv(0, st_v, j > 0);
+        if (more) {
+          ok = mbar_wait_bounded(&bars->kv_full[st_k], (it / L::kStages) & 1, abort_flag,
+                                 kTimeoutNs);
+          if (!ok) break;
+          tc_fence_after();
+          issue_qk(0, st_k);
+          mma_commit(&bars->s_full[0]);
+        } else {
+          mma_commit(&bars->o_final[0]);
+        }
+        // query tile 1
+        ok = mbar_wait_bounded(&bars->p_full[1], j & 1, abort_flag, kTimeoutNs);
+        if (!ok) break;
+        tc_fence_after();
+        issue_pv(1, st_v, j > 0);
+        mma_commit(&bars->kv_empty[st_v]);
+        if (more) {
+          issue_qk(1, st_k);
+          mma_commit(&bars->s_full[1]);
+          mma_commit(&bars->kv_empty[st_k]);
+          ++it;
+        } else {
+          mma_commit(&bars->o_final[1]);
+        }
+      }
+      if (!ok && !*abort_flag) report(p, TA_DEVSTAT_TIMEOUT_MMA, abort_flag);
+      // Drain: all MMAs this thread issued complete before tensor memory is freed.
+      mma_commit(&bars->drain);
+      volatile int no_abort = 0;
+      if (!mbar_wait_bounded(&bars->drain, 0, &no_abort, kTimeoutNs) && p.status)
+        atomicOr(p.status, TA_DEVSTAT_TIMEOUT_DRAIN);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ softmax + epilogue
+    const int t = warp >> 2;            // query tile of this warpgroup
+    const int quarter = warp & 3;       // TMEM lane quarter this warp may access
+    const int r_in_tile = quarter * 32 + lane;
+    const int tile_row0 = q_row0 + t * kRowsPerTile;
+    const int row = tile_row0 + r_in_tile;
+    const uint32_t lane_bits = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t t_s = tmem + lane_bits + t * 128;
+    const uint32_t t_o = tmem + lane_bits + 256 + t * D;
+    const float sl = p.scale_log2;
+
+    float m_run = -INFINITY;  // running max, in log2 units (score * scale * log2 e)
+    float l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      ok = mbar_wait_bounded(&bars->s_full[t], j & 1, abort_flag, kTimeoutNs);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      float s[kKeysPerTile];
+      {
+        uint32_t r0[32], r1[32], r2[32], r3[32];
+        tmem_ld32(t_s + 0, r0);
+        tmem_ld32(t_s + 32, r1);
+        tmem_ld32(t_s + 64, r2);
+        tmem_ld32(t_s + 96, r3);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          s[i] = __uint_as_float(r0[i]);
+          s[32 + i] = __uint_as_float(r1[i]);
+          s[64 + i] = __uint_as_float(r2[i]);
+          s[96 + i] = __uint_as_float(r3[i]);
+        }
+      }
+      const int c0 = j * kKeysPerTile;
+      const bool need_mask =
+          (c0 + kKeysPerTile > S) || (CAUSAL && c0 + kKeysPerTile - 1 > tile_row0);
+      if (need_mask) {
+        int lim = S - c0;
+        if (CAUSAL) lim = min(lim, row - c0 + 1);
+#pragma unroll
+        for (int i = 0; i < kKeysPerTile; ++i)
+          if (i >= lim) s[i] = -INFINITY;
+      }
+      float mx0 = s[0], mx1 = s[1], mx2 = s[2], mx3 = s[3];
+#pragma unroll
+      for (int i = 4; i < kKeysPerTile; i += 4) {
+        mx0 = fmaxf(mx0, s[i]);
+        mx1 = fmaxf(mx1, s[i + 1]);
+        mx2 = fmaxf(mx2, s[i + 2]);
+        mx3 = fmaxf(mx3, s[i + 3]);
+      }
+      const float m_cand = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl;
+      if (j == 0) {
+        m_run = m_cand;
+      } else {
+        const bool grow = m_cand > m_run + kRescaleThreshold;
+        if (__any_sync(0xffffffffu, grow)) {
+          float alpha = 1.f;
+          if (grow) {
+            alpha = ex2_approx(m_run - m_cand);
+            l_run *= alpha;
+            m_run = m_cand;
+          }
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld32(t_o + c * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st32(t_o + c * 32, o);
+          }
+        }
+      }
+      const float neg_m = -m_run;
+      float sum0 = 0.f, sum1 = 0.f;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t pk[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float p0 = ex2_approx(fmaf(s[64 * half + 2 * i], sl, neg_m));
+          const float p1 = ex2_approx(fmaf(s[64 * half + 2 * i + 1], sl, neg_m));
+          pk[i] = pack2<BF16>(p0, p1);
+          // The row sum uses the rounded weights the P.V MMA sees, so the output is
+          // an exact convex combination of V rows with those weights.
+          float2 r = unpack2<BF16>(pk[i]);
+          sum0 += r.x;
+          sum1 += r.y;
+        }
+        tmem_st32(t_s + 32 * half, pk);
+      }
+      l_run += sum0 + sum1;
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&bars->p_full[t]);
+    }
+    if (!ok) {
+      if (lane == 0 && !*abort_flag) report(p, TA_DEVSTAT_TIMEOUT_SOFTMAX, abort_flag);
+    } else {
+      ok = mbar_wait_bounded(&bars->o_final[t], 0, abort_flag, kTimeoutNs);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) {
+        if (lane == 0 && !*abort_flag) report(p, TA_DEVSTAT_TIMEOUT_EPILOG, abort_flag);
+      } else {
+        tc_fence_after();
+        const float inv_l = 1.f / l_run;
+        const bool in_range = row < S;
+        uint8_t* orow = reinterpret_cast<uint8_t*>(p.o) +
+                        2 * (static_cast<int64_t>(b) * p.o_sb + static_cast<int64_t>(h) * p.o_sh +
+                             static_cast<int64_t>(row) * p.o_ss);
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(t_o + c * 32, o);
+          tmem_wait_ld();
+          uint32_t pw[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            pw[i] = pack2<BF16>(__uint_as_float(o[2 * i]) * inv_l,
+                                __uint_as_float(o[2 * i + 1]) * inv_l);
+          if (in_range) {
+            uint4* dst = reinterpret_cast<uint4*>(orow + c * 64);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              dst[i] = make_uint4(pw[4 * i], pw[4 * i + 1], pw[4 * i + 2], pw[4 * i + 3]);
+          }
+        }
+        if (p.lse != nullptr && in_range)
+          p.lse[static_cast<int64_t>(bh) * S + row] = (m_run + __log2f(l_run)) * 0.69314718055994531f;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == kMmaWarp) tmem_dealloc(tmem, kTmemCols);
+}
+
+template <int D, bool BF16, bool CAUSAL>
+static cudaError_t launch_variant(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
+                                  const FwdParams& p, int grid, cudaStream_t stream) {
+  auto kern = sdpa_fwd_kernel<D, BF16, CAUSAL>;
+  constexpr int smem = Layout<D>::kDynSmem;
+  static int configured_mask = 0;  // one bit per device ordinal (< 32)
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  if (dev >= 32 || !(__atomic_load_n(&configured_mask, __ATOMIC_ACQUIRE) & (1 << dev))) {
+    err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (err != cudaSuccess) return err;
+    if (dev < 32) __atomic_fetch_or(&configured_mask, 1 << dev, __ATOMIC_ACQ_REL);
+  }
+  kern<<<grid, kThreads, smem, stream>>>(q, k, v, p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_sdpa_fwd(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
+                            const FwdParams& p, int D, bool bf16, bool causal,
+                            cudaStream_t stream) {
+  const int grid = p.BH * p.n_qblk;
+  if (grid == 0) return cudaSuccess;
+#define TA_DISPATCH(DD, BB, CC)                                                   \
+  if (D == DD && bf16 == BB && causal == CC)                                      \
+    return launch_variant<DD, BB, CC>(q, k, v, p, grid, stream);
+  TA_DISPATCH(64, false, false)
+  TA_DISPATCH(64, false, true)
+  TA_DISPATCH(64, true, false)
+  TA_DISPATCH(64, true, true)
+  TA_DISPATCH(128, false, false)
+  TA_DISPATCH(128, false, true)
+  TA_DISPATCH(128, true, false)
+  TA_DISPATCH(128, true, true)
+#undef TA_DISPATCH
+  return cudaErrorInvalidValue;
+}
+
+int rows_per_cta() { return kRowsPerCta; }
+
+}  // namespace ta

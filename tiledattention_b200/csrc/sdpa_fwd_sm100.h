@@ -1,0 +1,28 @@
+// Internal interface between the C ABI (capi.cu) and the sm_100a kernels.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ta {
+
+struct FwdParams {
+  void* o;                 // output base pointer, [B,H,S,D]
+  float* lse;              // optional [B*H*S] natural-log log-sum-exp per row
+  unsigned int* status;    // optional device status word (TA_DEVSTAT_* bits)
+  int64_t o_sb, o_sh, o_ss;  // output element strides (dim stride is 1)
+  int S, H, BH, n_qblk;
+  float scale_log2;        // scale * log2(e)
+};
+
+// Query rows one CTA covers (two 128-row tiles).
+int rows_per_cta();
+
+// Launches the variant for (D, dtype, causal) on `stream`. Tensor maps are 4-D
+// (D, S, H, B) with a 64 x 128 box and 128-byte swizzle.
+cudaError_t launch_sdpa_fwd(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
+                            const FwdParams& p, int D, bool bf16, bool causal,
+                            cudaStream_t stream);
+
+}  // namespace ta

@@ -1,0 +1,151 @@
+"""Host launcher: layout policy, output allocation and the call through the C ABI.
+
+Replaces run_flash_fwd (src/tiledattention/kernels/flash_fwd.py:821-973) and
+_launch_cutile_kernel (flash_fwd.py:786-818) of the reference:
+  * no reshape / transpose copies: each operand keeps its own strides, which the C
+    ABI turns into TMA tensor maps; only layouts TMA cannot express (head-dim stride
+    != 1, strides or base not 16-byte aligned) are made contiguous first, as the
+    reference does unconditionally (flash_fwd.py:865-867);
+  * head dims other than 64/128 are zero-padded to the next supported size
+    (flash_fwd.py:149-163, 868-872); the scale is resolved by the caller from the
+    original head dim (sdpa.py:46-47), so padding does not change the result;
+  * the output is a fresh tensor like empty_like(q) (flash_fwd.py:877);
+  * the launch goes on torch's current stream of q's device (the reference launches
+    on CuPy's current stream, flash_fwd.py:805-809);
+  * TILEDATTN_SYNC_MODE = async (default) | post | strict keeps the reference's debug
+    sync semantics (flash_fwd.py:805-818); post/strict also read the kernel's device
+    status word and raise KernelError if a bounded wait in the kernel expired.
+"""
+
+from __future__ import annotations
+
+import os
+
+from . import _native, _runtime
+from ._errors import (
+    DTypeNotSupportedError,
+    InvalidShapeError,
+    KernelError,
+    UnsupportedPlatformError,
+)
+
+NATIVE_HEAD_DIMS = (64, 128)
+_status_words: dict[int, object] = {}
+
+
+def padded_head_dim(head_dim: int) -> int:
+    """Head dim the kernel runs at for a given input head dim."""
+    for d in NATIVE_HEAD_DIMS:
+        if head_dim <= d:
+            return d
+    raise InvalidShapeError(
+        f"head dim {head_dim} is not supported (this build supports head dims up to 128)."
+    )
+
+
+def _status_word(torch_mod, device):
+    idx = device.index if device.index is not None else torch_mod.cuda.current_device()
+    word = _status_words.get(idx)
+    if word is None:
+        word = torch_mod.zeros(1, dtype=torch_mod.int32, device=device)
+        _status_words[idx] = word
+    return word
+
+
+def check_device_status(device=None) -> None:
+    """Synchronise `device` and raise KernelError if a kernel reported a timeout."""
+    torch_mod = _runtime.get_torch_module()
+    if device is None:
+        device = torch_mod.device("cuda", torch_mod.cuda.current_device())
+    word = _status_word(torch_mod, torch_mod.device(device))
+    torch_mod.cuda.synchronize(word.device)
+    value = int(word.item())
+    if value:
+        word.zero_()
+        raise KernelError("tiledattention kernel: " + _native.describe_devstat(value))
+
+
+def _tma_compatible(t) -> bool:
+    if t.stride(-1) != 1 or t.data_ptr() % 16:
+        return False
+    for dim in range(3):
+        if t.size(dim) > 1 and (t.stride(dim) * t.element_size()) % 16:
+            return False
+    return True
+
+
+def _sync_mode() -> str:
+    mode = os.getenv("TILEDATTN_SYNC_MODE", "async").strip().lower()
+    return mode if mode in ("async", "post", "strict") else "async"
+
+
+def run_sdpa_fwd(q, k, v, *, causal: bool, scale: float, return_lse: bool = False):
+    """Launch the sm_100a kernel. Inputs are already validated ([B,H,S,D], fp16/bf16, CUDA).
+
+    Returns o (and the float32 [B,H,S] natural-log log-sum-exp when return_lse=True).
+    """
+    torch_mod = _runtime.get_torch_module()
+    lib = _runtime.get_native_library()
+    batch, heads, seq_len, head_dim = (int(x) for x in q.shape)
+    kdim = padded_head_dim(head_dim)
+    if q.dtype == torch_mod.float16:
+        dtype_code = _native.TA_DTYPE_F16
+    elif q.dtype == torch_mod.bfloat16:
+        dtype_code = _native.TA_DTYPE_BF16
+    else:  # validated earlier; kept for direct callers
+        raise DTypeNotSupportedError("q dtype must be torch.float16 or torch.bfloat16.")
+
+    out = torch_mod.empty((batch, heads, seq_len, kdim), dtype=q.dtype, device=q.device)
+    lse = None
+    if return_lse:
+        lse = torch_mod.empty((batch, heads, seq_len), dtype=torch_mod.float32, device=q.device)
+    if out.numel() == 0:
+        o = out[..., :head_dim] if kdim != head_dim else out
+        return (o, lse) if return_lse else o
+
+    if kdim != head_dim:
+        pad = (0, kdim - head_dim)
+        q = torch_mod.nn.functional.pad(q, pad)
+        k = torch_mod.nn.functional.pad(k, pad)
+        v = torch_mod.nn.functional.pad(v, pad)
+    q, k, v = (t if _tma_compatible(t) else t.contiguous() for t in (q, k, v))
+
+    mode = _sync_mode()
+    with torch_mod.cuda.device(q.device):
+        status = _status_word(torch_mod, q.device)
+        stream = torch_mod.cuda.current_stream(q.device).cuda_stream
+        if mode == "strict":
+            torch_mod.cuda.synchronize(q.device)
+        rc = lib.ta_sdpa_fwd(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+            lse.data_ptr() if lse is not None else None,
+            batch, heads, seq_len, kdim,
+            _native.strides4(q.stride()), _native.strides4(k.stride()),
+            _native.strides4(v.stride()), _native.strides4(out.stride()),
+            dtype_code, 1 if causal else 0, float(scale), status.data_ptr(), stream,
+        )
+        if rc == _native.TA_ERR_LAYOUT and not all(t.is_contiguous() for t in (q, k, v)):
+            q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+            rc = lib.ta_sdpa_fwd(
+                q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                lse.data_ptr() if lse is not None else None,
+                batch, heads, seq_len, kdim,
+                _native.strides4(q.stride()), _native.strides4(k.stride()),
+                _native.strides4(v.stride()), _native.strides4(out.stride()),
+                dtype_code, 1 if causal else 0, float(scale), status.data_ptr(), stream,
+            )
+        if rc != _native.TA_OK:
+            detail = _native.last_error(lib) or _native.status_string(lib, rc)
+            if rc == _native.TA_ERR_DEVICE:
+                raise UnsupportedPlatformError(detail)
+            if rc in (_native.TA_ERR_INVALID_ARGUMENT, _native.TA_ERR_UNSUPPORTED_DIM,
+                      _native.TA_ERR_LAYOUT):
+                raise InvalidShapeError(detail)
+            if rc == _native.TA_ERR_UNSUPPORTED_DTYPE:
+                raise DTypeNotSupportedError(detail)
+            raise KernelError(detail)
+        if mode in ("post", "strict"):
+            check_device_status(q.device)
+
+    o = out[..., :head_dim] if kdim != head_dim else out
+    return (o, lse) if return_lse else o
