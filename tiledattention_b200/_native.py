@@ -65,7 +65,8 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
     with _lock:
         if _lib is not None and path is None:
             return _lib
-        lib_path = path or LIB_PATH
+        # TILEDATTN_NATIVE_LIB: load another build of the same ABI (A/B experiments).
+        lib_path = path or os.environ.get("TILEDATTN_NATIVE_LIB") or LIB_PATH
         if not os.path.exists(lib_path):
             raise DependencyError(
                 f"native library {lib_path} not found; build it with "

@@ -21,6 +21,7 @@
 //   warps 4-7  softmax + epilogue for query tile 1
 //   warp  8    TMA producer: Q tiles once, then K_0, V_0, K_1, V_1 ... through a ring
 //   warp  9    TMEM allocator and single-thread tcgen05.mma issuer
+//   warps 10-11 idle (complete the third warpgroup for the register split)
 // Tensor memory: S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [256+D,256+2D) columns;
 // P_t (16-bit, two per column) overwrites the first 64 columns of S_t and feeds the
 // P.V MMA straight from tensor memory.
@@ -49,11 +50,26 @@ constexpr int kRowsPerTile = 128;  // query rows per tile (= TMEM lanes)
 constexpr int kTilesPerCta = 2;    // query tiles per CTA
 constexpr int kRowsPerCta = kRowsPerTile * kTilesPerCta;
 constexpr int kKeysPerTile = 128;  // keys per K/V tile
-constexpr int kThreads = 320;
+constexpr int kThreads = 384;
+// Register split: the kernel is built for kLaunchRegs per thread (launch bounds 384 x 1);
+// after start-up the producer/MMA warpgroup gives registers back (setmaxnreg.dec to
+// kSideRegs) and the two softmax warpgroups take them (setmaxnreg.inc to kSoftmaxRegs).
+// 2*128*kSoftmaxRegs + 128*kSideRegs == 384*kLaunchRegs, so the increase always fits
+// in the block's launch allocation; the host refuses to launch a build whose register
+// count differs from kLaunchRegs.
+constexpr int kLaunchRegs = 168;
+constexpr int kSoftmaxRegs = 216;
+constexpr int kSideRegs = 72;
+static_assert(2 * 128 * kSoftmaxRegs + 128 * kSideRegs == kThreads * kLaunchRegs,
+              "register split must match the launch allocation");
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;      // log2 units
+#ifndef TA_POLY_EVERY
+#define TA_POLY_EVERY 0
+#endif
+constexpr int kPolyEvery = TA_POLY_EVERY;  // every kPolyEvery-th element pair: exp2 on the FMA pipe
 constexpr uint64_t kTimeoutNs = 1000000000ull;  // 1 s per wait
 
 template <int D>
@@ -164,6 +180,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
 
+  // Each role branch starts with its warpgroup's setmaxnreg so that the register limit
+  // ptxas applies to the code after it is the one of that branch.
+  if (warp >= 8) {
+  regs_dec<kSideRegs>();
   if (warp == kProducerWarp) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
@@ -283,7 +303,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         atomicOr(p.status, TA_DEVSTAT_TIMEOUT_DRAIN);
     }
     __syncwarp();
+  }
   } else {
+    regs_inc<kSoftmaxRegs>();
     // ------------------------------------------------------------ softmax + epilogue
     const int t = warp >> 2;            // query tile of this warpgroup
     const int quarter = warp & 3;       // TMEM lane quarter this warp may access
@@ -329,13 +351,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < kKeysPerTile; ++i)
           if (i >= lim) s[i] = -INFINITY;
       }
-      float mx0 = s[0], mx1 = s[1], mx2 = s[2], mx3 = s[3];
+      // Row max: four independent chains of 3-input max.
+      float mx0 = fmaxf(s[0], s[1]), mx1 = fmaxf(s[2], s[3]);
+      float mx2 = fmaxf(s[4], s[5]), mx3 = fmaxf(s[6], s[7]);
 #pragma unroll
-      for (int i = 4; i < kKeysPerTile; i += 4) {
-        mx0 = fmaxf(mx0, s[i]);
-        mx1 = fmaxf(mx1, s[i + 1]);
-        mx2 = fmaxf(mx2, s[i + 2]);
-        mx3 = fmaxf(mx3, s[i + 3]);
+      for (int i = 8; i < kKeysPerTile; i += 8) {
+        mx0 = fmax3(mx0, s[i], s[i + 1]);
+        mx1 = fmax3(mx1, s[i + 2], s[i + 3]);
+        mx2 = fmax3(mx2, s[i + 4], s[i + 5]);
+        mx3 = fmax3(mx3, s[i + 6], s[i + 7]);
       }
       const float m_cand = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl;
       if (j == 0) {
@@ -349,36 +373,58 @@ __global__ void __launch_bounds__(kThreads, 1)
             l_run *= alpha;
             m_run = m_cand;
           }
+          const uint64_t alpha2 = f2_pack(alpha, alpha);
 #pragma unroll
           for (int c = 0; c < D / 32; ++c) {
             uint32_t o[32];
             tmem_ld32(t_o + c * 32, o);
             tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            for (int i = 0; i < 32; i += 2) {
+              float a0, a1;
+              f2_unpack(f2_mul(f2_pack(__uint_as_float(o[i]), __uint_as_float(o[i + 1])), alpha2),
+                        a0, a1);
+              o[i] = __float_as_uint(a0);
+              o[i + 1] = __float_as_uint(a1);
+            }
             tmem_st32(t_o + c * 32, o);
           }
         }
       }
-      const float neg_m = -m_run;
-      float sum0 = 0.f, sum1 = 0.f;
+      // p = 2^(s*scale*log2e - m): packed FMA, then exp2 on the MUFU for most pairs and
+      // on the FMA pipe (polynomial) for every kPolyEvery-th pair, to balance the pipes.
+      const uint64_t sl2 = f2_pack(sl, sl);
+      const uint64_t negm2 = f2_pack(-m_run, -m_run);
+      uint64_t sum2 = f2_pack(0.f, 0.f);
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         uint32_t pk[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const float p0 = ex2_approx(fmaf(s[64 * half + 2 * i], sl, neg_m));
-          const float p1 = ex2_approx(fmaf(s[64 * half + 2 * i + 1], sl, neg_m));
+          const int e = 64 * half + 2 * i;
+          const uint64_t x2 = f2_fma(f2_pack(s[e], s[e + 1]), sl2, negm2);
+          float p0, p1;
+          if (kPolyEvery > 0 && (i % (kPolyEvery > 0 ? kPolyEvery : 1)) == kPolyEvery - 1) {
+            f2_unpack(exp2_poly_x2(x2), p0, p1);
+          } else {
+            float x0, x1;
+            f2_unpack(x2, x0, x1);
+            p0 = ex2_approx(x0);
+            p1 = ex2_approx(x1);
+          }
           pk[i] = pack2<BF16>(p0, p1);
           // The row sum uses the rounded weights the P.V MMA sees, so the output is
           // an exact convex combination of V rows with those weights.
-          float2 r = unpack2<BF16>(pk[i]);
-          sum0 += r.x;
-          sum1 += r.y;
+          const float2 r = unpack2<BF16>(pk[i]);
+          sum2 = f2_add(sum2, f2_pack(r.x, r.y));
         }
         tmem_st32(t_s + 32 * half, pk);
       }
-      l_run += sum0 + sum1;
+      {
+        float a0, a1;
+        f2_unpack(sum2, a0, a1);
+        l_run += a0 + a1;
+      }
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&bars->p_full[t]);
@@ -436,6 +482,12 @@ static cudaError_t launch_variant(const CUtensorMap& q, const CUtensorMap& k, co
   cudaError_t err = cudaGetDevice(&dev);
   if (err != cudaSuccess) return err;
   if (dev >= 32 || !(__atomic_load_n(&configured_mask, __ATOMIC_ACQUIRE) & (1 << dev))) {
+    // setmaxnreg.inc would wait forever if the block were launched with fewer
+    // registers than the split assumes: check the built register count first.
+    cudaFuncAttributes attr;
+    err = cudaFuncGetAttributes(&attr, kern);
+    if (err != cudaSuccess) return err;
+    if (attr.numRegs != kLaunchRegs) return cudaErrorInvalidKernelImage;
     err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (err != cudaSuccess) return err;
     if (dev < 32) __atomic_fetch_or(&configured_mask, 1 << dev, __ATOMIC_ACQ_REL);

@@ -218,3 +218,76 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool bf16, bool a
 }
 
 }  // namespace ta
+
+namespace ta {
+
+// ------------------------------------------------------------------ packed fp32 / registers
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Warpgroup register re-balancing (all warps of a warpgroup execute the same one).
+template <uint32_t N>
+__device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+// 2^x for a pair of fp32 values on the FMA/ALU pipes (no MUFU):
+// Cody-Waite style reduction x = j + f, j = round(x), f in [-1/2, 1/2], then 2^f from a
+// degree-3 polynomial whose coefficients are a Remez (minimax relative error) fit of
+// 2^f on [-1/2, 1/2] computed for this project (max relative error 7.5e-5 = 2^-13.7),
+// and 2^j added straight into the exponent field. Inputs are clamped to >= -125, so
+// masked (-inf) scores give 2^-125 (~2e-38) rather than 0.
+__device__ __forceinline__ uint64_t exp2_poly_x2(uint64_t x2) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23: float add rounds to an integer
+  float x0, x1;
+  f2_unpack(x2, x0, x1);
+  x0 = fmaxf(x0, -125.f);
+  x1 = fmaxf(x1, -125.f);
+  const uint64_t xc = f2_pack(x0, x1);
+  const uint64_t t = f2_add(xc, f2_pack(kMagic, kMagic));
+  const uint64_t r = f2_add(t, f2_pack(-kMagic, -kMagic));
+  float r0, r1;
+  f2_unpack(r, r0, r1);
+  const uint64_t f = f2_add(xc, f2_pack(-r0, -r1));
+  uint64_t p = f2_fma(f2_pack(0.0551716685f, 0.0551716685f), f, f2_pack(0.242611125f, 0.242611125f));
+  p = f2_fma(p, f, f2_pack(0.693260968f, 0.693260968f));
+  p = f2_fma(p, f, f2_pack(0.999928057f, 0.999928057f));
+  float p0, p1, t0, t1;
+  f2_unpack(p, p0, p1);
+  f2_unpack(t, t0, t1);
+  const uint32_t e0 = __float_as_uint(t0) << 23;
+  const uint32_t e1 = __float_as_uint(t1) << 23;
+  return f2_pack(__uint_as_float(__float_as_uint(p0) + e0), __uint_as_float(__float_as_uint(p1) + e1));
+}
+
+}  // namespace ta
