@@ -101,9 +101,18 @@ int check_device() {
   return TA_OK;
 }
 
+#ifdef TA_TRACE
+unsigned long long* g_trace = nullptr;
+#endif
 }  // namespace
 
 extern "C" {
+
+#ifdef TA_TRACE
+// Experiment builds only (not part of the public header): device buffer for kernel
+// event clocks, 64 blocks x 32 key tiles x 16 events of uint64.
+void ta_debug_set_trace(void* dev_ptr) { g_trace = static_cast<unsigned long long*>(dev_ptr); }
+#endif
 
 int ta_abi_version(void) { return 100; }
 
@@ -172,6 +181,9 @@ int ta_sdpa_fwd(const void* q, const void* k, const void* v, void* o, float* lse
   p.BH = B * H;
   p.n_qblk = (S + ta::rows_per_cta() - 1) / ta::rows_per_cta();
   p.scale_log2 = static_cast<float>(static_cast<double>(scale) * 1.4426950408889634);
+#ifdef TA_TRACE
+  p.trace = g_trace;
+#endif
   if (static_cast<int64_t>(p.BH) * p.n_qblk > 0x7fffffffll)
     return fail(TA_ERR_INVALID_ARGUMENT, "grid too large");
 

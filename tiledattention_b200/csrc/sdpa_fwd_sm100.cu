@@ -66,6 +66,21 @@ constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;      // log2 units
+#ifndef TA_ROWSUM
+#define TA_ROWSUM 1  // 0: unpack + packed add, 1: mixed-precision add, 2: unrounded p
+#endif
+#ifdef TA_MMA_SPIN
+#define MMA_WAIT mbar_spin_bounded
+#else
+#define MMA_WAIT mbar_wait_bounded
+#endif
+#ifndef TA_ABL
+#define TA_ABL 0  // experiment switches (0 in the product build)
+#endif
+#ifndef TA_SUM_CHAINS
+#define TA_SUM_CHAINS 4
+#endif
+constexpr int kSumChains = TA_SUM_CHAINS;
 #ifndef TA_POLY_EVERY
 #define TA_POLY_EVERY 0
 #endif
@@ -102,6 +117,21 @@ __device__ __forceinline__ void report(const FwdParams& p, uint32_t code, volati
   if (p.status) atomicOr(p.status, code);
 }
 
+#ifdef TA_TRACE
+// Experiment builds only: clock64 of event `ev` (< 16) of key tile j (< 32) in the
+// first 64 blocks, for timeline analysis.
+__device__ __forceinline__ void trace_ev(const FwdParams& p, int j, int ev) {
+  if (p.trace && blockIdx.x < 64 && j < 32) {
+    unsigned long long c;
+    asm volatile("mov.u64 %0, %%clock64;" : "=l"(c));
+    p.trace[(blockIdx.x * 32 + j) * 16 + ev] = c;
+  }
+}
+#define TRACE(j, ev) trace_ev(p, (j), (ev))
+#else
+#define TRACE(j, ev)
+#endif
+
 // Two fp32 values -> one 32-bit word of two 16-bit values, `lo` in the low half.
 template <bool BF16>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
@@ -121,6 +151,19 @@ __device__ __forceinline__ float2 unpack2(uint32_t w) {
     __half2 h = *reinterpret_cast<__half2*>(&w);
     return __half22float2(h);
   }
+}
+
+// acc_lo += low 16-bit value of w, acc_hi += high one (fp32 accumulation of bf16/fp16).
+template <bool BF16>
+__device__ __forceinline__ void add_packed16_to_f32(uint32_t w, float& acc_lo, float& acc_hi) {
+  if constexpr (BF16)
+    asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
+        "add.rn.f32.bf16 %0, lo, %0;\n\tadd.rn.f32.bf16 %1, hi, %1;\n\t}"
+        : "+f"(acc_lo), "+f"(acc_hi) : "r"(w));
+  else
+    asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
+        "add.rn.f32.f16 %0, lo, %0;\n\tadd.rn.f32.f16 %1, hi, %1;\n\t}"
+        : "+f"(acc_lo), "+f"(acc_hi) : "r"(w));
 }
 
 template <int D, bool BF16, bool CAUSAL>
@@ -222,26 +265,30 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t kIdescQK = idesc_f16(kRowsPerTile, kKeysPerTile, BF16, false, false);
       constexpr uint32_t kIdescPV = idesc_f16(kRowsPerTile, D, BF16, false, true);
-      const uint32_t q_addr = smem_u32(q_smem);
-      const uint32_t kv_addr = smem_u32(kv_smem);
+      // Descriptors are built once; per K step only the start-address field (low bits)
+      // advances, by a compile-time constant, so issuing an MMA costs a 64-bit add.
+      const uint64_t q_desc = sdesc_sw128(smem_u32(q_smem), 16, 1024);
+      const uint64_t kv_desc_k = sdesc_sw128(smem_u32(kv_smem), 16, 1024);
+      const uint64_t kv_desc_v = sdesc_sw128(smem_u32(kv_smem), kKeysPerTile * 128, 1024);
       auto issue_qk = [&](int t, int st) {
-        const uint32_t qa = q_addr + t * L::kTileBytes;
-        const uint32_t ka = kv_addr + st * L::kTileBytes;
+        const uint64_t qd = q_desc + static_cast<uint64_t>((t * L::kTileBytes) >> 4);
+        const uint64_t kd = kv_desc_k + static_cast<uint64_t>((st * L::kTileBytes) >> 4);
+        const uint32_t d_tmem = tmem + t * 128;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * (kRowsPerTile * 128) + (kk & 3) * 32;
-          mma_ss(tmem + t * 128, sdesc_sw128(qa + off, 16, 1024), sdesc_sw128(ka + off, 16, 1024),
-                 kIdescQK, kk > 0 ? 1u : 0u);
+          constexpr int kAtom = kRowsPerTile * 128;
+          const uint64_t off = static_cast<uint64_t>(((kk >> 2) * kAtom + (kk & 3) * 32) >> 4);
+          mma_ss(d_tmem, qd + off, kd + off, kIdescQK, kk > 0 ? 1u : 0u);
         }
       };
       auto issue_pv = [&](int t, int st, bool acc) {
-        const uint32_t va = kv_addr + st * L::kTileBytes;
+        const uint64_t vd = kv_desc_v + static_cast<uint64_t>((st * L::kTileBytes) >> 4);
+        const uint32_t d_tmem = tmem + 256 + t * D;
+        const uint32_t a_tmem = tmem + t * 128;
 #pragma unroll
-        for (int kk = 0; kk < kKeysPerTile / 16; ++kk) {
-          mma_ts(tmem + 256 + t * D, tmem + t * 128 + kk * 8,
-                 sdesc_sw128(va + kk * 16 * 128, kKeysPerTile * 128, 1024), kIdescPV,
-                 (acc || kk > 0) ? 1u : 0u);
-        }
+        for (int kk = 0; kk < kKeysPerTile / 16; ++kk)
+          mma_ts(d_tmem, a_tmem + kk * 8, vd + static_cast<uint64_t>((kk * 16 * 128) >> 4),
+                 kIdescPV, (acc || kk > 0) ? 1u : 0u);
       };
       bool ok = mbar_wait_bounded(&bars->q_full, 0, abort_flag, kTimeoutNs);
       int it = 0;
@@ -266,8 +313,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool more = (j + 1 < n_kv);
         const int st_k = it % L::kStages;
         // query tile 0
-        ok = mbar_wait_bounded(&bars->p_full[0], j & 1, abort_flag, kTimeoutNs);
+        ok = MMA_WAIT(&bars->p_full[0], j & 1, abort_flag, kTimeoutNs);
         if (!ok) break;
+        TRACE(j, 8);
         tc_fence_after();
         issue_pv(0, st_v, j > 0);
         if (more) {
@@ -281,8 +329,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma_commit(&bars->o_final[0]);
         }
         // query tile 1
-        ok = mbar_wait_bounded(&bars->p_full[1], j & 1, abort_flag, kTimeoutNs);
+        TRACE(j, 9);
+        ok = MMA_WAIT(&bars->p_full[1], j & 1, abort_flag, kTimeoutNs);
         if (!ok) break;
+        TRACE(j, 10);
         tc_fence_after();
         issue_pv(1, st_v, j > 0);
         mma_commit(&bars->kv_empty[st_v]);
@@ -294,6 +344,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else {
           mma_commit(&bars->o_final[1]);
         }
+        TRACE(j, 11);
       }
       if (!ok && !*abort_flag) report(p, TA_DEVSTAT_TIMEOUT_MMA, abort_flag);
       // Drain: all MMAs this thread issued complete before tensor memory is freed.
@@ -325,6 +376,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
+      if (threadIdx.x % 128 == 0) TRACE(j, 0 + 4 * t);
+#if TA_ABL & 8
+      tc_fence_before();
+      mbar_arrive(&bars->p_full[t]);
+      continue;
+#endif
       float s[kKeysPerTile];
       {
         uint32_t r0[32], r1[32], r2[32], r3[32];
@@ -341,6 +398,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           s[96 + i] = __uint_as_float(r3[i]);
         }
       }
+      if (threadIdx.x % 128 == 0) TRACE(j, 1 + 4 * t);
       const int c0 = j * kKeysPerTile;
       const bool need_mask =
           (c0 + kKeysPerTile > S) || (CAUSAL && c0 + kKeysPerTile - 1 > tile_row0);
@@ -393,40 +451,67 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // p = 2^(s*scale*log2e - m): packed FMA, then exp2 on the MUFU for most pairs and
       // on the FMA pipe (polynomial) for every kPolyEvery-th pair, to balance the pipes.
+      if (threadIdx.x % 128 == 0) TRACE(j, 2 + 4 * t);
       const uint64_t sl2 = f2_pack(sl, sl);
       const uint64_t negm2 = f2_pack(-m_run, -m_run);
-      uint64_t sum2 = f2_pack(0.f, 0.f);
+      // Row sum in kSumChains independent fp32 accumulator pairs (short dependency chains).
+      float acc_lo[kSumChains], acc_hi[kSumChains];
+#pragma unroll
+      for (int c = 0; c < kSumChains; ++c) acc_lo[c] = acc_hi[c] = 0.f;
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         uint32_t pk[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const int e = 64 * half + 2 * i;
-          const uint64_t x2 = f2_fma(f2_pack(s[e], s[e + 1]), sl2, negm2);
           float p0, p1;
+#if TA_ABL & 2
+          const float x0 = fmaf(s[e], sl, -m_run), x1 = fmaf(s[e + 1], sl, -m_run);
+          p0 = ex2_approx(x0);
+          p1 = ex2_approx(x1);
+#else
+          const uint64_t x2 = f2_fma(f2_pack(s[e], s[e + 1]), sl2, negm2);
           if (kPolyEvery > 0 && (i % (kPolyEvery > 0 ? kPolyEvery : 1)) == kPolyEvery - 1) {
             f2_unpack(exp2_poly_x2(x2), p0, p1);
           } else {
             float x0, x1;
             f2_unpack(x2, x0, x1);
+#if TA_ABL & 4
+            p0 = x0; p1 = x1;
+#else
             p0 = ex2_approx(x0);
             p1 = ex2_approx(x1);
+#endif
           }
+#endif
           pk[i] = pack2<BF16>(p0, p1);
+#if TA_ABL & 1
+#elif TA_ROWSUM == 0
           // The row sum uses the rounded weights the P.V MMA sees, so the output is
           // an exact convex combination of V rows with those weights.
-          const float2 r = unpack2<BF16>(pk[i]);
-          sum2 = f2_add(sum2, f2_pack(r.x, r.y));
+          {
+            const float2 r = unpack2<BF16>(pk[i]);
+            acc_lo[i % kSumChains] += r.x;
+            acc_hi[i % kSumChains] += r.y;
+          }
+#elif TA_ROWSUM == 1
+          add_packed16_to_f32<BF16>(pk[i], acc_lo[i % kSumChains], acc_hi[i % kSumChains]);
+#else
+          acc_lo[i % kSumChains] += p0;
+          acc_hi[i % kSumChains] += p1;
+#endif
         }
         tmem_st32(t_s + 32 * half, pk);
       }
       {
-        float a0, a1;
-        f2_unpack(sum2, a0, a1);
-        l_run += a0 + a1;
+        float tot = 0.f;
+#pragma unroll
+        for (int c = 0; c < kSumChains; ++c) tot += acc_lo[c] + acc_hi[c];
+        l_run += tot;
       }
       tmem_wait_st();
       tc_fence_before();
+      if (threadIdx.x % 128 == 0) TRACE(j, 3 + 4 * t);
       mbar_arrive(&bars->p_full[t]);
     }
     if (!ok) {

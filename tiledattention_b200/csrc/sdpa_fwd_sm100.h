@@ -14,6 +14,7 @@ struct FwdParams {
   int64_t o_sb, o_sh, o_ss;  // output element strides (dim stride is 1)
   int S, H, BH, n_qblk;
   float scale_log2;        // scale * log2(e)
+  unsigned long long* trace;  // experiment builds (-DTA_TRACE) only: event clocks
 };
 
 // Query rows one CTA covers (two 128-row tiles).
