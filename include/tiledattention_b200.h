@@ -46,6 +46,7 @@ extern "C" {
 /* Element types (match the reference's accepted dtypes, checks.py:50-55). */
 #define TA_DTYPE_F16  0
 #define TA_DTYPE_BF16 1
+#define TA_DTYPE_F32  2   /* only as the output type of ta_lse_combine */
 
 /* Device status word bits, written by the kernel with atomicOr when a bounded wait
  * inside the kernel expires (the kernel then drains its in-flight copies and MMAs,
@@ -82,6 +83,36 @@ int ta_sdpa_fwd(const void* q, const void* k, const void* v, void* o, float* lse
                 const int64_t* v_strides, const int64_t* o_strides,
                 int dtype, int causal, float scale,
                 unsigned int* dev_status, void* stream);
+
+/*
+ * ta_sdpa_fwd_partial — split-KV forward: the keys [kv_begin, kv_end) are cut into n_split
+ * slices of whole 128-key tiles (slice length ceil((kv_end-kv_begin)/n_split) rounded up to
+ * 128; trailing slices may be empty) and each slice is attended separately, in one launch.
+ *
+ *   o_part    device fp32 [n_split][B][H][S][D], contiguous: slice s's output normalised
+ *             by its own row sum (0 for rows with no valid key in the slice)
+ *   lse_part  device fp32 [n_split][B*H*S]: slice s's natural-log log-sum-exp per row
+ *             (-inf for rows with no valid key in the slice)
+ * Other arguments as for ta_sdpa_fwd. Merge with ta_lse_combine (same GPU) or across GPUs.
+ * The reference has no split-KV mode; this is the basis of the long-context path
+ * (per-slice online-softmax states, flash_fwd.py:405-436, merged by log-sum-exp).
+ */
+int ta_sdpa_fwd_partial(const void* q, const void* k, const void* v, float* o_part,
+                        float* lse_part, int B, int H, int S, int D,
+                        const int64_t* q_strides, const int64_t* k_strides,
+                        const int64_t* v_strides, int dtype, int causal, float scale,
+                        int kv_begin, int kv_end, int n_split,
+                        unsigned int* dev_status, void* stream);
+
+/*
+ * ta_lse_combine — merge n_split partial results (layout of ta_sdpa_fwd_partial) into
+ * o [B,H,S,D] (element strides o_strides, dtype TA_DTYPE_F16 / BF16 / F32) and optional
+ * lse [B*H*S]:  lse = log sum_s exp(lse_s),  o = sum_s exp(lse_s - lse) o_s.
+ * No counterpart in the reference (which has no split-KV mode). Allocates nothing.
+ */
+int ta_lse_combine(const float* o_part, const float* lse_part, int n_split,
+                   int B, int H, int S, int D, void* o, const int64_t* o_strides,
+                   int out_dtype, float* lse, void* stream);
 
 /*
  * ta_device_supported — 1 if `device` is a compute-capability 10.0 GPU this build runs

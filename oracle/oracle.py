@@ -61,8 +61,10 @@ def _to_f32(x) -> np.ndarray:
 
 
 def sdpa_numpy(q, k, v, *, causal: bool, scale: float, block: int = 256,
-               return_lse: bool = False):
-    """float64 restatement; q,k,v [B,H,S,D]. Returns float32 [B,H,S,D] (and lse [B,H,S])."""
+               return_lse: bool = False, kv_range: tuple[int, int] | None = None):
+    """float64 restatement; q,k,v [B,H,S,D]. Returns float32 [B,H,S,D] (and lse [B,H,S]).
+    kv_range=(lo, hi) restricts the keys to [lo, hi) (split-KV partial state); rows with no
+    valid key then give o = 0 and lse = -inf."""
     q, k, v = (_to_f32(t).astype(np.float64) for t in (q, k, v))
     B, H, S, D = q.shape
     out = np.empty((B, H, S, D), dtype=np.float64)
@@ -71,14 +73,19 @@ def sdpa_numpy(q, k, v, *, causal: bool, scale: float, block: int = 256,
     for r0 in range(0, S, block):
         r1 = min(S, r0 + block)
         s = np.einsum("bhrd,bhcd->bhrc", q[:, :, r0:r1], k) * scale
+        valid = np.ones((r1 - r0, S), dtype=bool)
         if causal:
-            rows = np.arange(r0, r1)[:, None]
-            s = np.where(cols[None, :] <= rows, s, -np.inf)
+            valid &= cols[None, :] <= np.arange(r0, r1)[:, None]
+        if kv_range is not None:
+            valid &= (cols[None, :] >= kv_range[0]) & (cols[None, :] < kv_range[1])
+        s = np.where(valid, s, -np.inf)
         m = s.max(axis=-1, keepdims=True)
-        p = np.exp(s - m)
+        m_safe = np.where(np.isfinite(m), m, 0.0)
+        p = np.exp(s - m_safe)
         l = p.sum(axis=-1, keepdims=True)
-        out[:, :, r0:r1] = np.einsum("bhrc,bhcd->bhrd", p, v) / l
-        lse[:, :, r0:r1] = (m + np.log(l))[..., 0]
+        with np.errstate(invalid="ignore", divide="ignore"):
+            out[:, :, r0:r1] = np.where(l > 0, np.einsum("bhrc,bhcd->bhrd", p, v) / l, 0.0)
+            lse[:, :, r0:r1] = np.where(l > 0, m_safe + np.log(l), -np.inf)[..., 0]
     if return_lse:
         return out.astype(np.float32), lse.astype(np.float32)
     return out.astype(np.float32)

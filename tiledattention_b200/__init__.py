@@ -20,12 +20,14 @@ from ._errors import (
 )
 from ._version import __version__
 from .launch import check_device_status
-from .sdpa import sdpa, sdpa_with_lse
+from .sdpa import sdpa, sdpa_partial, sdpa_split_kv, sdpa_with_lse
 
 __all__ = [
     "__version__",
     "sdpa",
     "sdpa_with_lse",
+    "sdpa_split_kv",
+    "sdpa_partial",
     "check_device_status",
     "TiledAttentionError",
     "UnsupportedPlatformError",

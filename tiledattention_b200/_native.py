@@ -28,6 +28,7 @@ TA_ERR_DEVICE = 7
 
 TA_DTYPE_F16 = 0
 TA_DTYPE_BF16 = 1
+TA_DTYPE_F32 = 2
 
 DEVSTAT_BITS = {
     1: "TMA producer wait timed out",
@@ -47,6 +48,24 @@ SIGNATURES = {
             ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
             _I64P, _I64P, _I64P, _I64P,
             ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p,
+        ],
+    ),
+    "ta_sdpa_fwd_partial": (
+        ctypes.c_int,
+        [
+            ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+            ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+            _I64P, _I64P, _I64P,
+            ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+            ctypes.c_void_p, ctypes.c_void_p,
+        ],
+    ),
+    "ta_lse_combine": (
+        ctypes.c_int,
+        [
+            ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+            ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+            ctypes.c_void_p, _I64P, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
         ],
     ),
     "ta_device_supported": (ctypes.c_int, [ctypes.c_int]),

@@ -17,6 +17,7 @@
 #include <mutex>
 #include <string>
 
+#include "lse_combine.h"
 #include "sdpa_fwd_sm100.h"
 #include "tiledattention_b200.h"
 
@@ -141,11 +142,13 @@ int ta_device_supported(int device) {
   return (major == 10 && minor == 0) ? 1 : 0;
 }
 
-int ta_sdpa_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int B, int H,
-                int S, int D, const int64_t* q_strides, const int64_t* k_strides,
-                const int64_t* v_strides, const int64_t* o_strides, int dtype, int causal,
-                float scale, unsigned int* dev_status, void* stream) {
-  g_last_error.clear();
+// Shared body of the forward entry points: argument checks, tensor maps, launch.
+static int run_forward(const void* q, const void* k, const void* v, void* o, bool out_f32,
+                       const int64_t* o_strides, int64_t o_split_stride, float* lse, int B,
+                       int H, int S, int D, const int64_t* q_strides, const int64_t* k_strides,
+                       const int64_t* v_strides, int dtype, int causal, float scale,
+                       int kv_begin, int kv_end, int n_split, unsigned int* dev_status,
+                       void* stream) {
   if (!q || !k || !v || !o || !q_strides || !k_strides || !v_strides || !o_strides)
     return fail(TA_ERR_INVALID_ARGUMENT, "null pointer argument");
   if (B <= 0 || H <= 0 || S <= 0)
@@ -155,9 +158,14 @@ int ta_sdpa_fwd(const void* q, const void* k, const void* v, void* o, float* lse
     return fail(TA_ERR_UNSUPPORTED_DTYPE, "dtype code %d", dtype);
   if (!(scale > 0.f) || !std::isfinite(scale))
     return fail(TA_ERR_INVALID_ARGUMENT, "scale must be a positive finite number");
+  if (kv_begin < 0 || kv_end > S || kv_begin > kv_end)
+    return fail(TA_ERR_INVALID_ARGUMENT, "key range [%d, %d) outside [0, %d]", kv_begin, kv_end, S);
+  if (n_split < 1 || n_split > 4096)
+    return fail(TA_ERR_INVALID_ARGUMENT, "n_split must be in [1, 4096] (got %d)", n_split);
+  const int64_t esz = out_f32 ? 4 : 2;
   if (o_strides[3] != 1) return fail(TA_ERR_LAYOUT, "o: head-dim stride must be 1");
-  if (reinterpret_cast<uintptr_t>(o) % 16 || (o_strides[2] * 2) % 16 || (o_strides[1] * 2) % 16 ||
-      (o_strides[0] * 2) % 16)
+  if (reinterpret_cast<uintptr_t>(o) % 16 || (o_strides[2] * esz) % 16 ||
+      (o_strides[1] * esz) % 16 || (o_strides[0] * esz) % 16 || (o_split_stride * esz) % 16)
     return fail(TA_ERR_LAYOUT, "o: base / strides must be 16-byte aligned");
   if (static_cast<int64_t>(B) * H > (1ll << 24))
     return fail(TA_ERR_INVALID_ARGUMENT, "B*H too large");
@@ -176,21 +184,85 @@ int ta_sdpa_fwd(const void* q, const void* k, const void* v, void* o, float* lse
   p.o_sb = o_strides[0];
   p.o_sh = o_strides[1];
   p.o_ss = o_strides[2];
+  p.o_split_stride = o_split_stride;
   p.S = S;
   p.H = H;
   p.BH = B * H;
+  p.kv_begin = kv_begin;
+  p.kv_end = kv_end;
+  p.n_split = n_split;
+  // Slices are whole 128-key tiles, so only the last one can be ragged.
+  const int span = kv_end - kv_begin;
+  p.split_len = ((span + n_split - 1) / n_split + 127) / 128 * 128;
+  if (p.split_len == 0) p.split_len = 128;
   p.n_qblk = (S + ta::rows_per_cta() - 1) / ta::rows_per_cta();
   p.scale_log2 = static_cast<float>(static_cast<double>(scale) * 1.4426950408889634);
 #ifdef TA_TRACE
   p.trace = g_trace;
 #endif
-  if (static_cast<int64_t>(p.BH) * p.n_qblk > 0x7fffffffll)
-    return fail(TA_ERR_INVALID_ARGUMENT, "grid too large");
-
   cudaError_t err = ta::launch_sdpa_fwd(mq, mk, mv, p, D, dtype == TA_DTYPE_BF16, causal != 0,
-                                        static_cast<cudaStream_t>(stream));
+                                        out_f32, static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess)
     return fail(TA_ERR_CUDA, "kernel launch failed: %s", cudaGetErrorString(err));
+  return TA_OK;
+}
+
+int ta_sdpa_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int B, int H,
+                int S, int D, const int64_t* q_strides, const int64_t* k_strides,
+                const int64_t* v_strides, const int64_t* o_strides, int dtype, int causal,
+                float scale, unsigned int* dev_status, void* stream) {
+  g_last_error.clear();
+  return run_forward(q, k, v, o, false, o_strides, 0, lse, B, H, S, D, q_strides, k_strides,
+                     v_strides, dtype, causal, scale, 0, S, 1, dev_status, stream);
+}
+
+int ta_sdpa_fwd_partial(const void* q, const void* k, const void* v, float* o_part,
+                        float* lse_part, int B, int H, int S, int D, const int64_t* q_strides,
+                        const int64_t* k_strides, const int64_t* v_strides, int dtype,
+                        int causal, float scale, int kv_begin, int kv_end, int n_split,
+                        unsigned int* dev_status, void* stream) {
+  g_last_error.clear();
+  if (!lse_part) return fail(TA_ERR_INVALID_ARGUMENT, "lse_part must not be null");
+  const int64_t st[4] = {static_cast<int64_t>(H) * S * D, static_cast<int64_t>(S) * D, D, 1};
+  return run_forward(q, k, v, o_part, true, st, static_cast<int64_t>(B) * H * S * D, lse_part, B,
+                     H, S, D, q_strides, k_strides, v_strides, dtype, causal, scale, kv_begin,
+                     kv_end, n_split, dev_status, stream);
+}
+
+int ta_lse_combine(const float* o_part, const float* lse_part, int n_split, int B, int H, int S,
+                   int D, void* o, const int64_t* o_strides, int out_dtype, float* lse,
+                   void* stream) {
+  g_last_error.clear();
+  if (!o_part || !lse_part || !o || !o_strides)
+    return fail(TA_ERR_INVALID_ARGUMENT, "null pointer argument");
+  if (B <= 0 || H <= 0 || S <= 0 || n_split < 1)
+    return fail(TA_ERR_INVALID_ARGUMENT, "B, H, S, n_split must be positive");
+  if (D != 64 && D != 128) return fail(TA_ERR_UNSUPPORTED_DIM, "head dim %d not in {64, 128}", D);
+  if (out_dtype != TA_DTYPE_F16 && out_dtype != TA_DTYPE_BF16 && out_dtype != TA_DTYPE_F32)
+    return fail(TA_ERR_UNSUPPORTED_DTYPE, "output dtype code %d", out_dtype);
+  const int64_t esz = out_dtype == TA_DTYPE_F32 ? 4 : 2;
+  if (o_strides[3] != 1 || reinterpret_cast<uintptr_t>(o) % 16 ||
+      reinterpret_cast<uintptr_t>(o_part) % 16 || (o_strides[2] * esz) % 8 ||
+      (o_strides[1] * esz) % 8 || (o_strides[0] * esz) % 8)
+    return fail(TA_ERR_LAYOUT, "o: unit head-dim stride, aligned base and strides required");
+  int rc = check_device();
+  if (rc) return rc;
+  ta::CombineParams p{};
+  p.o_part = o_part;
+  p.lse_part = lse_part;
+  p.o = o;
+  p.lse = lse;
+  p.o_sb = o_strides[0];
+  p.o_sh = o_strides[1];
+  p.o_ss = o_strides[2];
+  p.n_split = n_split;
+  p.BH = B * H;
+  p.H = H;
+  p.S = S;
+  const int kind = out_dtype == TA_DTYPE_F32 ? 2 : (out_dtype == TA_DTYPE_BF16 ? 1 : 0);
+  cudaError_t err = ta::launch_lse_combine(p, D, kind, static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess)
+    return fail(TA_ERR_CUDA, "combine launch failed: %s", cudaGetErrorString(err));
   return TA_OK;
 }
 

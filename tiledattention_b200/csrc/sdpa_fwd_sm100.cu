@@ -166,7 +166,10 @@ __device__ __forceinline__ void add_packed16_to_f32(uint32_t w, float& acc_lo, f
         : "+f"(acc_lo), "+f"(acc_hi) : "r"(w));
 }
 
-template <int D, bool BF16, bool CAUSAL>
+// OUT_F32: write o as fp32 (the normalised partial output of one key slice) instead of
+// the input dtype. Grid = n_split x B*H x n_qblk; slice s covers keys
+// [kv_begin + s*split_len, min(kv_end, kv_begin + (s+1)*split_len)).
+template <int D, bool BF16, bool CAUSAL, bool OUT_F32>
 __global__ void __launch_bounds__(kThreads, 1)
     sdpa_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q,
                     const __grid_constant__ CUtensorMap tmap_k,
@@ -185,14 +188,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // Block -> (bh, query block). Consecutive blocks share a (b,h) so its K/V stays in L2;
   // inside a (b,h) the longest causal rows are issued first.
-  const int bh = blockIdx.x / p.n_qblk;
-  const int qblk = p.n_qblk - 1 - (blockIdx.x % p.n_qblk);
+  const int per_split = p.BH * p.n_qblk;
+  const int split = blockIdx.x / per_split;
+  const int blk = blockIdx.x - split * per_split;
+  const int bh = blk / p.n_qblk;
+  const int qblk = p.n_qblk - 1 - (blk % p.n_qblk);
   const int b = bh / p.H;
   const int h = bh % p.H;
   const int S = p.S;
+  // keys [kv_lo, kv_hi) take part (the whole range, or one slice for split-KV)
+  const int kv_lo = min(p.kv_end, p.kv_begin + split * p.split_len);
+  const int kv_hi = min(p.kv_end, kv_lo + p.split_len);
   const int q_row0 = qblk * kRowsPerCta;
-  const int kv_rows = CAUSAL ? min(S, q_row0 + kRowsPerCta) : S;
-  const int n_kv = (kv_rows + kKeysPerTile - 1) / kKeysPerTile;
+  const int kv_rows = CAUSAL ? min(kv_hi, q_row0 + kRowsPerCta) : kv_hi;
+  const int n_kv = kv_rows > kv_lo ? (kv_rows - kv_lo + kKeysPerTile - 1) / kKeysPerTile : 0;
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
@@ -245,7 +254,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mbar_arrive_expect_tx(&bars->kv_full[st], L::kTileBytes);
         const CUtensorMap* map = (it & 1) ? &tmap_v : &tmap_k;
-        const int key0 = (it >> 1) * kKeysPerTile;
+        const int key0 = kv_lo + (it >> 1) * kKeysPerTile;
         for (int c = 0; c < L::kChunks; ++c)
           tma_load_4d(kv_smem + st * L::kTileBytes + c * (kKeysPerTile * 128), map,
                       &bars->kv_full[st], c * 64, key0, h, b);
@@ -290,9 +299,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma_ts(d_tmem, a_tmem + kk * 8, vd + static_cast<uint64_t>((kk * 16 * 128) >> 4),
                  kIdescPV, (acc || kk > 0) ? 1u : 0u);
       };
-      bool ok = mbar_wait_bounded(&bars->q_full, 0, abort_flag, kTimeoutNs);
+      bool ok = true;
       int it = 0;
-      if (ok) {
+      if (n_kv > 0) ok = mbar_wait_bounded(&bars->q_full, 0, abort_flag, kTimeoutNs);
+      if (ok && n_kv > 0) {
         const int st = 0;
         ok = mbar_wait_bounded(&bars->kv_full[st], 0, abort_flag, kTimeoutNs);
         if (ok) {
@@ -399,11 +409,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (threadIdx.x % 128 == 0) TRACE(j, 1 + 4 * t);
-      const int c0 = j * kKeysPerTile;
+      const int c0 = kv_lo + j * kKeysPerTile;  // absolute index of the tile's first key
       const bool need_mask =
-          (c0 + kKeysPerTile > S) || (CAUSAL && c0 + kKeysPerTile - 1 > tile_row0);
+          (c0 + kKeysPerTile > kv_hi) || (CAUSAL && c0 + kKeysPerTile - 1 > tile_row0);
       if (need_mask) {
-        int lim = S - c0;
+        int lim = kv_hi - c0;
         if (CAUSAL) lim = min(lim, row - c0 + 1);
 #pragma unroll
         for (int i = 0; i < kKeysPerTile; ++i)
@@ -427,7 +437,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (__any_sync(0xffffffffu, grow)) {
           float alpha = 1.f;
           if (grow) {
-            alpha = ex2_approx(m_run - m_cand);
+            alpha = ex2_approx(m_run - m_cand);  // 0 while m_run is -inf
             l_run *= alpha;
             m_run = m_cand;
           }
@@ -452,8 +462,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       // p = 2^(s*scale*log2e - m): packed FMA, then exp2 on the MUFU for most pairs and
       // on the FMA pipe (polynomial) for every kPolyEvery-th pair, to balance the pipes.
       if (threadIdx.x % 128 == 0) TRACE(j, 2 + 4 * t);
+      // A row with no valid key yet (m = -inf; only possible with a key slice) uses 0 as
+      // the subtrahend, so its weights are exactly 0 instead of NaN.
+      const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
       const uint64_t sl2 = f2_pack(sl, sl);
-      const uint64_t negm2 = f2_pack(-m_run, -m_run);
+      const uint64_t negm2 = f2_pack(-m_use, -m_use);
       // Row sum in kSumChains independent fp32 accumulator pairs (short dependency chains).
       float acc_lo[kSumChains], acc_hi[kSumChains];
 #pragma unroll
@@ -517,36 +530,58 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!ok) {
       if (lane == 0 && !*abort_flag) report(p, TA_DEVSTAT_TIMEOUT_SOFTMAX, abort_flag);
     } else {
-      ok = mbar_wait_bounded(&bars->o_final[t], 0, abort_flag, kTimeoutNs);
-      ok = __all_sync(0xffffffffu, ok);
+      if (n_kv > 0) {
+        ok = mbar_wait_bounded(&bars->o_final[t], 0, abort_flag, kTimeoutNs);
+        ok = __all_sync(0xffffffffu, ok);
+      }
       if (!ok) {
         if (lane == 0 && !*abort_flag) report(p, TA_DEVSTAT_TIMEOUT_EPILOG, abort_flag);
       } else {
         tc_fence_after();
-        const float inv_l = 1.f / l_run;
+        // Rows without any valid key (only with a key slice) get o = 0 and lse = -inf.
+        const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
         const bool in_range = row < S;
+        constexpr int kOutBytes = OUT_F32 ? 4 : 2;
         uint8_t* orow = reinterpret_cast<uint8_t*>(p.o) +
-                        2 * (static_cast<int64_t>(b) * p.o_sb + static_cast<int64_t>(h) * p.o_sh +
-                             static_cast<int64_t>(row) * p.o_ss);
+                        kOutBytes * (static_cast<int64_t>(split) * p.o_split_stride +
+                                     static_cast<int64_t>(b) * p.o_sb +
+                                     static_cast<int64_t>(h) * p.o_sh +
+                                     static_cast<int64_t>(row) * p.o_ss);
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
           uint32_t o[32];
-          tmem_ld32(t_o + c * 32, o);
-          tmem_wait_ld();
-          uint32_t pw[16];
+          if (n_kv > 0) {
+            tmem_ld32(t_o + c * 32, o);
+            tmem_wait_ld();
+          } else {
 #pragma unroll
-          for (int i = 0; i < 16; ++i)
-            pw[i] = pack2<BF16>(__uint_as_float(o[2 * i]) * inv_l,
-                                __uint_as_float(o[2 * i + 1]) * inv_l);
-          if (in_range) {
-            uint4* dst = reinterpret_cast<uint4*>(orow + c * 64);
+            for (int i = 0; i < 32; ++i) o[i] = 0u;
+          }
+          if constexpr (OUT_F32) {
+            if (in_range) {
+              float4* dst = reinterpret_cast<float4*>(orow + c * 128);
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-              dst[i] = make_uint4(pw[4 * i], pw[4 * i + 1], pw[4 * i + 2], pw[4 * i + 3]);
+              for (int i = 0; i < 8; ++i)
+                dst[i] = make_float4(__uint_as_float(o[4 * i]) * inv_l, __uint_as_float(o[4 * i + 1]) * inv_l,
+                                     __uint_as_float(o[4 * i + 2]) * inv_l, __uint_as_float(o[4 * i + 3]) * inv_l);
+            }
+          } else {
+            uint32_t pw[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              pw[i] = pack2<BF16>(__uint_as_float(o[2 * i]) * inv_l,
+                                  __uint_as_float(o[2 * i + 1]) * inv_l);
+            if (in_range) {
+              uint4* dst = reinterpret_cast<uint4*>(orow + c * 64);
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                dst[i] = make_uint4(pw[4 * i], pw[4 * i + 1], pw[4 * i + 2], pw[4 * i + 3]);
+            }
           }
         }
         if (p.lse != nullptr && in_range)
-          p.lse[static_cast<int64_t>(bh) * S + row] = (m_run + __log2f(l_run)) * 0.69314718055994531f;
+          p.lse[static_cast<int64_t>(split) * p.BH * S + static_cast<int64_t>(bh) * S + row] =
+              l_run > 0.f ? (m_run + __log2f(l_run)) * 0.69314718055994531f : -INFINITY;
       }
     }
   }
@@ -557,10 +592,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == kMmaWarp) tmem_dealloc(tmem, kTmemCols);
 }
 
-template <int D, bool BF16, bool CAUSAL>
+template <int D, bool BF16, bool CAUSAL, bool OUT_F32>
 static cudaError_t launch_variant(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
                                   const FwdParams& p, int grid, cudaStream_t stream) {
-  auto kern = sdpa_fwd_kernel<D, BF16, CAUSAL>;
+  auto kern = sdpa_fwd_kernel<D, BF16, CAUSAL, OUT_F32>;
   constexpr int smem = Layout<D>::kDynSmem;
   static int configured_mask = 0;  // one bit per device ordinal (< 32)
   int dev = 0;
@@ -582,21 +617,24 @@ static cudaError_t launch_variant(const CUtensorMap& q, const CUtensorMap& k, co
 }
 
 cudaError_t launch_sdpa_fwd(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
-                            const FwdParams& p, int D, bool bf16, bool causal,
+                            const FwdParams& p, int D, bool bf16, bool causal, bool out_f32,
                             cudaStream_t stream) {
-  const int grid = p.BH * p.n_qblk;
+  const long long grid = static_cast<long long>(p.n_split) * p.BH * p.n_qblk;
   if (grid == 0) return cudaSuccess;
-#define TA_DISPATCH(DD, BB, CC)                                                   \
-  if (D == DD && bf16 == BB && causal == CC)                                      \
-    return launch_variant<DD, BB, CC>(q, k, v, p, grid, stream);
-  TA_DISPATCH(64, false, false)
-  TA_DISPATCH(64, false, true)
-  TA_DISPATCH(64, true, false)
-  TA_DISPATCH(64, true, true)
-  TA_DISPATCH(128, false, false)
-  TA_DISPATCH(128, false, true)
-  TA_DISPATCH(128, true, false)
-  TA_DISPATCH(128, true, true)
+  if (grid > 0x7fffffffll) return cudaErrorInvalidValue;
+#define TA_DISPATCH(DD, BB, CC, FF)                                               \
+  if (D == DD && bf16 == BB && causal == CC && out_f32 == FF)                     \
+    return launch_variant<DD, BB, CC, FF>(q, k, v, p, static_cast<int>(grid), stream);
+#define TA_DISPATCH2(DD, BB, CC) TA_DISPATCH(DD, BB, CC, false) TA_DISPATCH(DD, BB, CC, true)
+  TA_DISPATCH2(64, false, false)
+  TA_DISPATCH2(64, false, true)
+  TA_DISPATCH2(64, true, false)
+  TA_DISPATCH2(64, true, true)
+  TA_DISPATCH2(128, false, false)
+  TA_DISPATCH2(128, false, true)
+  TA_DISPATCH2(128, true, false)
+  TA_DISPATCH2(128, true, true)
+#undef TA_DISPATCH2
 #undef TA_DISPATCH
   return cudaErrorInvalidValue;
 }

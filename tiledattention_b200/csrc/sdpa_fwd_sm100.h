@@ -13,6 +13,9 @@ struct FwdParams {
   unsigned int* status;    // optional device status word (TA_DEVSTAT_* bits)
   int64_t o_sb, o_sh, o_ss;  // output element strides (dim stride is 1)
   int S, H, BH, n_qblk;
+  int kv_begin, kv_end;    // keys [kv_begin, kv_end) take part (0, S for full attention)
+  int n_split, split_len;  // key slices per launch (grid dim) and keys per slice
+  int64_t o_split_stride;  // output element stride between slices (partial mode)
   float scale_log2;        // scale * log2(e)
   unsigned long long* trace;  // experiment builds (-DTA_TRACE) only: event clocks
 };
@@ -23,7 +26,7 @@ int rows_per_cta();
 // Launches the variant for (D, dtype, causal) on `stream`. Tensor maps are 4-D
 // (D, S, H, B) with a 64 x 128 box and 128-byte swizzle.
 cudaError_t launch_sdpa_fwd(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
-                            const FwdParams& p, int D, bool bf16, bool causal,
+                            const FwdParams& p, int D, bool bf16, bool causal, bool out_f32,
                             cudaStream_t stream);
 
 }  // namespace ta

@@ -149,3 +149,89 @@ def run_sdpa_fwd(q, k, v, *, causal: bool, scale: float, return_lse: bool = Fals
 
     o = out[..., :head_dim] if kdim != head_dim else out
     return (o, lse) if return_lse else o
+
+
+def _dtype_code(torch_mod, dtype):
+    if dtype == torch_mod.float16:
+        return _native.TA_DTYPE_F16
+    if dtype == torch_mod.bfloat16:
+        return _native.TA_DTYPE_BF16
+    raise DTypeNotSupportedError("q dtype must be torch.float16 or torch.bfloat16.")
+
+
+def _raise_for(lib, rc):
+    detail = _native.last_error(lib) or _native.status_string(lib, rc)
+    if rc == _native.TA_ERR_DEVICE:
+        raise UnsupportedPlatformError(detail)
+    if rc in (_native.TA_ERR_INVALID_ARGUMENT, _native.TA_ERR_UNSUPPORTED_DIM, _native.TA_ERR_LAYOUT):
+        raise InvalidShapeError(detail)
+    if rc == _native.TA_ERR_UNSUPPORTED_DTYPE:
+        raise DTypeNotSupportedError(detail)
+    raise KernelError(detail)
+
+
+def run_sdpa_partial(q, k, v, *, causal: bool, scale: float, kv_begin: int = 0,
+                     kv_end: int | None = None, n_split: int = 1):
+    """Split-KV forward over keys [kv_begin, kv_end) cut into n_split slices.
+
+    Returns (o_part, lse_part): fp32 [n_split, B, H, S, Dk] (each slice normalised by its
+    own row sum) and fp32 [n_split, B, H, S] natural-log log-sum-exp (-inf where a slice
+    has no valid key for the row). Dk is the kernel head dim (64 or 128); padded head
+    dims are sliced off by the caller. Inputs are already validated.
+    """
+    torch_mod = _runtime.get_torch_module()
+    lib = _runtime.get_native_library()
+    batch, heads, seq_len, head_dim = (int(x) for x in q.shape)
+    kdim = padded_head_dim(head_dim)
+    kv_end = seq_len if kv_end is None else int(kv_end)
+    dtype_code = _dtype_code(torch_mod, q.dtype)
+    o_part = torch_mod.empty((n_split, batch, heads, seq_len, kdim), dtype=torch_mod.float32,
+                             device=q.device)
+    lse_part = torch_mod.empty((n_split, batch, heads, seq_len), dtype=torch_mod.float32,
+                               device=q.device)
+    if o_part.numel() == 0:
+        return o_part, lse_part
+    if kdim != head_dim:
+        pad = (0, kdim - head_dim)
+        q, k, v = (torch_mod.nn.functional.pad(t, pad) for t in (q, k, v))
+    q, k, v = (t if _tma_compatible(t) else t.contiguous() for t in (q, k, v))
+    with torch_mod.cuda.device(q.device):
+        status = _status_word(torch_mod, q.device)
+        stream = torch_mod.cuda.current_stream(q.device).cuda_stream
+        rc = lib.ta_sdpa_fwd_partial(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), o_part.data_ptr(), lse_part.data_ptr(),
+            batch, heads, seq_len, kdim,
+            _native.strides4(q.stride()), _native.strides4(k.stride()), _native.strides4(v.stride()),
+            dtype_code, 1 if causal else 0, float(scale), int(kv_begin), int(kv_end), int(n_split),
+            status.data_ptr(), stream,
+        )
+        if rc != _native.TA_OK:
+            _raise_for(lib, rc)
+        if _sync_mode() in ("post", "strict"):
+            check_device_status(q.device)
+    return o_part, lse_part
+
+
+def run_lse_combine(o_part, lse_part, *, out_dtype, head_dim: int | None = None,
+                    return_lse: bool = False):
+    """Merge split-KV partials (layout of run_sdpa_partial) on the GPU into o [B,H,S,D]
+    of out_dtype (float16 / bfloat16 / float32) and, optionally, lse [B,H,S]."""
+    torch_mod = _runtime.get_torch_module()
+    lib = _runtime.get_native_library()
+    n_split, batch, heads, seq_len, kdim = (int(x) for x in o_part.shape)
+    o = torch_mod.empty((batch, heads, seq_len, kdim), dtype=out_dtype, device=o_part.device)
+    lse = torch_mod.empty((batch, heads, seq_len), dtype=torch_mod.float32, device=o_part.device)
+    code = _native.TA_DTYPE_F32 if out_dtype == torch_mod.float32 else _dtype_code(torch_mod, out_dtype)
+    if o.numel() > 0:
+        o_part = o_part.contiguous()
+        lse_part = lse_part.contiguous()
+        with torch_mod.cuda.device(o_part.device):
+            stream = torch_mod.cuda.current_stream(o_part.device).cuda_stream
+            rc = lib.ta_lse_combine(o_part.data_ptr(), lse_part.data_ptr(), n_split, batch, heads,
+                                    seq_len, kdim, o.data_ptr(), _native.strides4(o.stride()),
+                                    code, lse.data_ptr() if return_lse else None, stream)
+            if rc != _native.TA_OK:
+                _raise_for(lib, rc)
+    if head_dim is not None and head_dim != kdim:
+        o = o[..., :head_dim]
+    return (o, lse) if return_lse else o

@@ -14,7 +14,7 @@ from numbers import Real
 from . import _runtime
 from ._errors import InvalidShapeError
 from .checks import validate_sdpa_inputs
-from .launch import run_sdpa_fwd
+from .launch import run_lse_combine, run_sdpa_fwd, run_sdpa_partial
 
 
 def _prepare(q, k, v, causal, scale):
@@ -49,3 +49,31 @@ def sdpa_with_lse(q, k, v, *, causal: bool = False, scale: float | None = None):
     """
     resolved_scale = _prepare(q, k, v, causal, scale)
     return run_sdpa_fwd(q, k, v, causal=causal, scale=resolved_scale, return_lse=True)
+
+
+def sdpa_split_kv(q, k, v, *, causal: bool = False, scale: float | None = None,
+                  n_split: int = 4, return_lse: bool = False):
+    """sdpa computed as n_split key slices in one launch plus a log-sum-exp merge.
+
+    Same result as sdpa (up to fp32 rounding); useful when B*H*ceil(S/256) is small
+    compared with the 148 SMs of a B200 (long sequences with few heads, decode-like
+    shapes). The reference has no split-KV mode.
+    """
+    resolved_scale = _prepare(q, k, v, causal, scale)
+    if not isinstance(n_split, int) or n_split < 1:
+        raise InvalidShapeError("n_split must be a positive int.")
+    o_part, lse_part = run_sdpa_partial(q, k, v, causal=causal, scale=resolved_scale,
+                                        n_split=n_split)
+    return run_lse_combine(o_part, lse_part, out_dtype=q.dtype, head_dim=int(q.shape[-1]),
+                           return_lse=return_lse)
+
+
+def sdpa_partial(q, k, v, *, causal: bool = False, scale: float | None = None,
+                 kv_begin: int = 0, kv_end: int | None = None, n_split: int = 1):
+    """Attention of all query rows over the keys [kv_begin, kv_end) only (split into
+    n_split slices): returns fp32 (o_part [n_split,B,H,S,D], lse_part [n_split,B,H,S])."""
+    resolved_scale = _prepare(q, k, v, causal, scale)
+    o_part, lse_part = run_sdpa_partial(q, k, v, causal=causal, scale=resolved_scale,
+                                        kv_begin=kv_begin, kv_end=kv_end, n_split=n_split)
+    head_dim = int(q.shape[-1])
+    return (o_part[..., :head_dim] if o_part.shape[-1] != head_dim else o_part), lse_part
