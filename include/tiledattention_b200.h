@@ -115,6 +115,28 @@ int ta_lse_combine(const float* o_part, const float* lse_part, int n_split,
                    int out_dtype, float* lse, void* stream);
 
 /*
+ * ta_sdpa_fwd_split_noalloc — the split-KV forward (ta_sdpa_fwd_partial over all keys in
+ * n_split slices, then ta_lse_combine into o / lse) for callers that cannot allocate
+ * device memory around the attention call: plugins handed only their inputs and outputs
+ * by a host application that owns the GPU memory, and latency-critical loops where a
+ * cudaMalloc could synchronise or fail. It allocates nothing: the slice partials live in a
+ * fixed 64 MiB array in device global memory that the library reserves on every GPU that
+ * loads it, until the process exits. Limits: n_split*B*H*S*(D+1)*4 bytes must fit in
+ * 64 MiB (else TA_ERR_INVALID_ARGUMENT); the first call on a device looks up the array's
+ * device address and should happen before any stream capture on that device; all calls on
+ * a device share the array, so calls that overlap on the GPU race — order them (one
+ * stream). Nothing needs clearing between calls: each call rewrites every entry it reads.
+ * Arguments as for ta_sdpa_fwd (o: dtype of q; lse optional). No counterpart in the
+ * reference.
+ */
+int ta_sdpa_fwd_split_noalloc(const void* q, const void* k, const void* v, void* o, float* lse,
+                              int B, int H, int S, int D,
+                              const int64_t* q_strides, const int64_t* k_strides,
+                              const int64_t* v_strides, const int64_t* o_strides,
+                              int dtype, int causal, float scale, int n_split,
+                              unsigned int* dev_status, void* stream);
+
+/*
  * ta_device_supported — 1 if `device` is a compute-capability 10.0 GPU this build runs
  * on, 0 otherwise. Replaces the runtime gate require_supported_runtime
  * (src/tiledattention/_runtime.py:161-191), narrowed to the sm_100a build.

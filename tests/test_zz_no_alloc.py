@@ -1,0 +1,72 @@
+"""The allocation-free split-KV entry point, ta_sdpa_fwd_split_noalloc, called through the
+C ABI. It exists for callers that cannot allocate device memory around the attention call
+(a plugin given only its inputs and outputs by a host that owns the GPU memory, or a
+latency-critical loop where cudaMalloc could synchronise or fail); its slice partials live
+in a fixed array inside the library instead of a per-call buffer.
+
+The test compares it, on two calls in a row (the second reuses the scratch array the first
+one filled), with the regular entry point ta_sdpa_fwd on the same inputs, within the
+tolerance of the parity tests. It lives in its own file named to be collected last."""
+
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+TOL = {torch.float16: 2e-3, torch.bfloat16: 1e-2}
+RTOL = {torch.float16: 2.0 ** -10, torch.bfloat16: 2.0 ** -8}
+
+
+def _strides(t):
+    from tiledattention_b200 import _native
+
+    return _native.strides4(t.stride())
+
+
+def test_noalloc_split_matches_regular_entry_point_twice():
+    from tiledattention_b200 import _native
+
+    lib = _native.load_library()
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    cases = [
+        (torch.bfloat16, 1, 4, 3001, 128, True, 4),   # ragged S, causal
+        (torch.float16, 2, 2, 1000, 64, False, 3),     # non-causal, head dim 64
+    ]
+    for call in range(2):
+        for dtype, B, H, S, D, causal, n_split in cases:
+            g = torch.Generator().manual_seed(100 * call + S)
+            q, k, v = (torch.randn(B, H, S, D, generator=g).to(dtype).to(dev) for _ in range(3))
+            code = _native.TA_DTYPE_BF16 if dtype == torch.bfloat16 else _native.TA_DTYPE_F16
+            scale = 1.0 / math.sqrt(D)
+            o_ref = torch.empty_like(q)
+            o_new = torch.full_like(q, float("nan"))
+            rc = lib.ta_sdpa_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o_ref.data_ptr(), None,
+                                 B, H, S, D, _strides(q), _strides(k), _strides(v), _strides(o_ref),
+                                 code, int(causal), scale, None, stream)
+            assert rc == 0, _native.last_error(lib)
+            rc = lib.ta_sdpa_fwd_split_noalloc(
+                q.data_ptr(), k.data_ptr(), v.data_ptr(), o_new.data_ptr(), None,
+                B, H, S, D, _strides(q), _strides(k), _strides(v), _strides(o_new),
+                code, int(causal), scale, n_split, None, stream)
+            assert rc == 0, _native.last_error(lib)
+            torch.cuda.synchronize(dev)
+            ref, got = o_ref.float(), o_new.float()
+            assert torch.isfinite(got).all()
+            bound = TOL[dtype] + RTOL[dtype] * ref.abs()
+            assert float(((got - ref).abs() - bound).max()) <= 0, float((got - ref).abs().max())
+
+
+def test_noalloc_split_rejects_oversized_problem():
+    from tiledattention_b200 import _native
+
+    lib = _native.load_library()
+    st = _native.strides4([16 * 65536 * 128, 65536 * 128, 128, 1])
+    # 8 slices x 16 heads x 65536 rows x 129 floats is far beyond the 64 MiB array
+    rc = lib.ta_sdpa_fwd_split_noalloc(16, 16, 16, 16, None, 1, 16, 65536, 128, st, st, st, st,
+                                       _native.TA_DTYPE_BF16, 1, 0.1, 8, None, None)
+    assert rc == _native.TA_ERR_INVALID_ARGUMENT
+    assert "64 MiB" in _native.last_error(lib)

@@ -68,6 +68,16 @@ SIGNATURES = {
             ctypes.c_void_p, _I64P, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
         ],
     ),
+    "ta_sdpa_fwd_split_noalloc": (
+        ctypes.c_int,
+        [
+            ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+            ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+            _I64P, _I64P, _I64P, _I64P,
+            ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_int,
+            ctypes.c_void_p, ctypes.c_void_p,
+        ],
+    ),
     "ta_device_supported": (ctypes.c_int, [ctypes.c_int]),
     "ta_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "ta_last_error": (ctypes.c_char_p, []),

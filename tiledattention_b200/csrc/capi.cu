@@ -17,6 +17,7 @@
 #include <mutex>
 #include <string>
 
+#include "capi_internal.h"
 #include "lse_combine.h"
 #include "sdpa_fwd_sm100.h"
 #include "tiledattention_b200.h"
@@ -107,6 +108,9 @@ unsigned long long* g_trace = nullptr;
 #endif
 }  // namespace
 
+int ta_capi_fail(int code, const char* msg) { return fail(code, "%s", msg); }
+void ta_capi_clear_error() { g_last_error.clear(); }
+
 extern "C" {
 
 #ifdef TA_TRACE
@@ -142,8 +146,10 @@ int ta_device_supported(int device) {
   return (major == 10 && minor == 0) ? 1 : 0;
 }
 
+}  // extern "C"
+
 // Shared body of the forward entry points: argument checks, tensor maps, launch.
-static int run_forward(const void* q, const void* k, const void* v, void* o, bool out_f32,
+int run_forward(const void* q, const void* k, const void* v, void* o, bool out_f32,
                        const int64_t* o_strides, int64_t o_split_stride, float* lse, int B,
                        int H, int S, int D, const int64_t* q_strides, const int64_t* k_strides,
                        const int64_t* v_strides, int dtype, int causal, float scale,
@@ -206,6 +212,8 @@ static int run_forward(const void* q, const void* k, const void* v, void* o, boo
     return fail(TA_ERR_CUDA, "kernel launch failed: %s", cudaGetErrorString(err));
   return TA_OK;
 }
+
+extern "C" {
 
 int ta_sdpa_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int B, int H,
                 int S, int D, const int64_t* q_strides, const int64_t* k_strides,
