@@ -58,8 +58,12 @@ constexpr int kThreads = 384;
 // in the block's launch allocation; the host refuses to launch a build whose register
 // count differs from kLaunchRegs.
 constexpr int kLaunchRegs = 168;
-constexpr int kSoftmaxRegs = 216;
-constexpr int kSideRegs = 72;
+#ifndef TA_SOFTMAX_REGS
+#define TA_SOFTMAX_REGS 208
+#define TA_SIDE_REGS 88
+#endif
+constexpr int kSoftmaxRegs = TA_SOFTMAX_REGS;
+constexpr int kSideRegs = TA_SIDE_REGS;
 static_assert(2 * 128 * kSoftmaxRegs + 128 * kSideRegs == kThreads * kLaunchRegs,
               "register split must match the launch allocation");
 constexpr int kProducerWarp = 8;
