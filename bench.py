@@ -53,12 +53,6 @@ def flops(B, H, S, D, causal):
     return 2.0 * B * H * S * (S + 1) * D if causal else 4.0 * B * H * S * S * D
 
 
-def shard_pairs(n_pairs, world, rank):
-    base, rem = divmod(n_pairs, world)
-    start = rank * base + min(rank, rem)
-    return start, base + (1 if rank < rem else 0)
-
-
 def measured_peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -244,6 +238,7 @@ def main():
     import torch.distributed as dist
 
     import tiledattention_b200 as ta
+    from tiledattention_b200.distributed import shard_pairs
 
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
