@@ -41,8 +41,15 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
-WORKLOAD = {"name": "llama_prefill_b8_h32_s4096_d128_bf16_causal",
-            "B": 8, "H": 32, "S": 4096, "D": 128, "causal": True, "dtype": "bf16"}
+WORKLOADS = {
+    # BASELINE config 3 (the metric's workload; default)
+    "llama_prefill": {"name": "llama_prefill_b8_h32_s4096_d128_bf16_causal",
+                      "B": 8, "H": 32, "S": 4096, "D": 128, "causal": True, "dtype": "bf16"},
+    # BASELINE config 5 (long context)
+    "long_context": {"name": "long_context_b1_h16_s65536_d128_bf16_causal",
+                     "B": 1, "H": 16, "S": 65536, "D": 128, "causal": True, "dtype": "bf16"},
+}
+WORKLOAD = WORKLOADS["llama_prefill"]
 SEED = 1234
 FALLBACK_PEAK_TFLOPS = 1590.0
 L2_FLUSH_BYTES = 256 << 20
@@ -221,6 +228,11 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="llama_prefill")
+    ap.add_argument("--mode", choices=["bh", "split_kv"], default="bh",
+                    help="bh: shard (batch, head) pairs over ranks, no collective; split_kv: "
+                         "every rank takes zig-zag key slices of all pairs, NCCL log-sum-exp "
+                         "merge inside the timed step (n_split=4 slices on one GPU)")
     ap.add_argument("--pairs", type=int, default=0,
                     help="profiling case: run only this many of the 256 (b,h) pairs")
     args = ap.parse_args()
@@ -245,13 +257,27 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", device_id=device)
 
-    wl = WORKLOAD
+    wl = WORKLOADS[args.workload]
     B, H, S, D, causal = wl["B"], wl["H"], wl["S"], wl["D"], wl["causal"]
     dtype = torch.bfloat16
     n_pairs = args.pairs if 0 < args.pairs < B * H else B * H
-    pair_start, pairs = shard_pairs(n_pairs, world, rank)
+    if args.mode == "split_kv":
+        pair_start, pairs = 0, n_pairs  # every rank holds all pairs, splits the keys
+        if world > 1:
+            from tiledattention_b200.distributed import sdpa_split_kv_distributed
+
+            def step_fn(q_, k_, v_):
+                return sdpa_split_kv_distributed(q_, k_, v_, causal=causal)[0]
+        else:
+            def step_fn(q_, k_, v_):
+                return ta.sdpa_split_kv(q_, k_, v_, causal=causal, n_split=4)
+    else:
+        pair_start, pairs = shard_pairs(n_pairs, world, rank)
+
+        def step_fn(q_, k_, v_):
+            return ta.sdpa(q_, k_, v_, causal=causal)
     q, k, v = make_inputs(torch, pairs, S, D, dtype, pair_start, device=device)
-    step_flops = flops(1, pairs, S, D, causal)
+    step_flops = flops(1, pairs, S, D, causal) / (world if args.mode == "split_kv" else 1)
     job_flops = flops(1, n_pairs, S, D, causal)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     stream = torch.cuda.current_stream(device)
@@ -270,7 +296,7 @@ def main():
     sampler = ClockSampler(device.index if device.index is not None else 0)
     for _ in range(args.warmup):
         flush.zero_()
-        o = ta.sdpa(q, k, v, causal=causal)
+        o = step_fn(q, k, v)
     torch.cuda.synchronize(device)
     ta.check_device_status(device)
 
@@ -282,7 +308,7 @@ def main():
     for i in range(args.steps):
         flush.zero_()  # L2 flush, enqueued before the start event: not timed
         starts[i].record(stream)
-        o = ta.sdpa(q, k, v, causal=causal)
+        o = step_fn(q, k, v)
         ends[i].record(stream)
     torch.cuda.synchronize(device)
     barrier()
@@ -302,7 +328,7 @@ def main():
     for _ in range(2):
         for d, h in ((dq, hq), (dk, hk), (dv, hv)):
             d.copy_(h, non_blocking=True)
-        ho.copy_(ta.sdpa(dq, dk, dv, causal=causal), non_blocking=True)
+        ho.copy_(step_fn(dq, dk, dv), non_blocking=True)
     torch.cuda.synchronize(device)
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -310,15 +336,16 @@ def main():
     for _ in range(e_steps):
         for d, h in ((dq, hq), (dk, hk), (dv, hv)):
             d.copy_(h, non_blocking=True)
-        ho.copy_(ta.sdpa(dq, dk, dv, causal=causal), non_blocking=True)
+        ho.copy_(step_fn(dq, dk, dv), non_blocking=True)
     e1.record(stream)
     torch.cuda.synchronize(device)
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1))
     e2e_value = job_flops * e_steps / (e2e_ms / 1e3) / 1e12
     elem = 2
-    h2d = 3 * n_pairs * S * D * elem
-    d2h = n_pairs * S * D * elem
+    copies = world if args.mode == "split_kv" else 1  # split_kv: every rank copies all pairs
+    h2d = 3 * n_pairs * S * D * elem * copies
+    d2h = n_pairs * S * D * elem * copies
 
     if rank != 0:
         if world > 1:
@@ -328,10 +355,11 @@ def main():
     peaks, peak_kind = measured_peaks()
     peak = float(peaks.get("bf16_tflops", FALLBACK_PEAK_TFLOPS))
     achieved = step_flops / (avg_launch_ms / 1e3) / 1e12
-    traffic = ncu_traffic_per_launch() if world == 1 else None
+    traffic = (ncu_traffic_per_launch()
+               if world == 1 and args.workload == "llama_prefill" and args.mode == "bh" else None)
 
     cpu = None
-    if world == 1 and not args.no_cpu_baseline:
+    if world == 1 and not args.no_cpu_baseline and args.workload == "llama_prefill":
         v_cpu, desc, cores, _ = cpu_sample(S, D, causal, float(os.environ.get("TA_CPU_SAMPLE_S", "10")))
         cpu = {"value": round(v_cpu, 5), "unit": "TFLOP/s", "cores": cores, "kind": "port",
                "sample": desc}
@@ -351,7 +379,8 @@ def main():
         "data": "synthetic N(0,1), seeded per (b,h) pair",
         "config": {"workload": wl["name"] if n_pairs == B * H else f"{wl['name']}[{n_pairs} pairs]",
                    "B": B, "H": H, "S": S, "D": D, "causal": causal,
-                   "pairs_per_gpu": pairs, "parallelism": f"bh-shard{world}",
+                   "pairs_per_gpu": pairs,
+                   "parallelism": (f"bh-shard{world}" if args.mode == "bh" else f"split-kv{world}"),
                    "l2": "256 MB L2 flush enqueued before every timed step",
                    "pct_of_bf16_peak": round(100 * value / world / peak, 2)},
         "e2e": {"value": round(e2e_value, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
@@ -363,7 +392,7 @@ def main():
                      "traffic": traffic},
         "cpu_baseline": cpu,
         "clocks": clocks,
-        "gpu_launches": args.steps * world,
+        "gpu_launches": args.steps * world * (1 if args.mode == "bh" else (3 if world > 1 else 2)),
     }
     print(json.dumps(line), flush=True)
     if world > 1:
