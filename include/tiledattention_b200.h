@@ -149,6 +149,16 @@ const char* ta_status_string(int status);
 /* ta_last_error — text of the last failure on the calling host thread ("" if none). */
 const char* ta_last_error(void);
 
+/*
+ * ta_debug_set_selftest — test hook for the failure path, process-wide, off by default.
+ * timeout_ns (0 = 1 s) limits every wait inside the kernels launched afterwards; with
+ * stall = 1 the MMA warp first waits on a barrier nothing arrives on, so that wait runs
+ * out: the kernel sets TA_DEVSTAT_TIMEOUT_MMA in dev_status, drains its copies, frees its
+ * tensor memory and returns, leaving the context usable. Never faults or hangs the GPU.
+ * Call ta_debug_set_selftest(0, 0) to restore normal operation. No reference counterpart.
+ */
+void ta_debug_set_selftest(int stall, unsigned long long timeout_ns);
+
 /* ta_abi_version — ABI version of this library (major*100 + minor). */
 int ta_abi_version(void);
 

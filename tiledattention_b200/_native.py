@@ -82,6 +82,7 @@ SIGNATURES = {
     "ta_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "ta_last_error": (ctypes.c_char_p, []),
     "ta_abi_version": (ctypes.c_int, []),
+    "ta_debug_set_selftest": (None, [ctypes.c_int, ctypes.c_ulonglong]),
 }
 
 _lib = None

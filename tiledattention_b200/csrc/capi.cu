@@ -14,6 +14,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 #include <string>
 
@@ -106,6 +107,9 @@ int check_device() {
 #ifdef TA_TRACE
 unsigned long long* g_trace = nullptr;
 #endif
+// Failure-path self-test settings (ta_debug_set_selftest); off by default.
+std::atomic<int> g_selftest_stall{0};
+std::atomic<unsigned long long> g_timeout_ns{0};
 }  // namespace
 
 int ta_capi_fail(int code, const char* msg) { return fail(code, "%s", msg); }
@@ -120,6 +124,11 @@ void ta_debug_set_trace(void* dev_ptr) { g_trace = static_cast<unsigned long lon
 #endif
 
 int ta_abi_version(void) { return 100; }
+
+void ta_debug_set_selftest(int stall, unsigned long long timeout_ns) {
+  g_selftest_stall.store(stall ? 1 : 0);
+  g_timeout_ns.store(timeout_ns);
+}
 
 const char* ta_last_error(void) { return g_last_error.c_str(); }
 
@@ -206,6 +215,8 @@ int run_forward(const void* q, const void* k, const void* v, void* o, bool out_f
 #ifdef TA_TRACE
   p.trace = g_trace;
 #endif
+  p.timeout_ns = g_timeout_ns.load();
+  p.selftest_stall = g_selftest_stall.load();
   cudaError_t err = ta::launch_sdpa_fwd(mq, mk, mv, p, D, dtype == TA_DTYPE_BF16, causal != 0,
                                         out_f32, static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess)

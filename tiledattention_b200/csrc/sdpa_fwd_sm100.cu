@@ -89,7 +89,7 @@ constexpr int kSumChains = TA_SUM_CHAINS;
 #define TA_POLY_EVERY 0
 #endif
 constexpr int kPolyEvery = TA_POLY_EVERY;  // every kPolyEvery-th element pair: exp2 on the FMA pipe
-constexpr uint64_t kTimeoutNs = 1000000000ull;  // 1 s per wait
+constexpr uint64_t kDefaultTimeoutNs = 1000000000ull;  // 1 s per wait
 
 template <int D>
 struct Layout {
@@ -109,6 +109,7 @@ struct Barriers {
   uint64_t p_full[2];
   uint64_t o_final[2];
   uint64_t drain;
+  uint64_t never;     // self-test only: a barrier nothing arrives on
   uint64_t kv_full[8];
   uint64_t kv_empty[8];
   uint32_t tmem_base;
@@ -186,6 +187,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* kv_smem = smem + L::kKVOff;
   Barriers* bars = reinterpret_cast<Barriers*>(smem + L::kBarOff);
   volatile int* abort_flag = &bars->abort_flag;
+  const uint64_t kTimeoutNs = p.timeout_ns ? p.timeout_ns : kDefaultTimeoutNs;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -215,6 +217,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars->o_final[t], 1);
     }
     mbar_init(&bars->drain, 1);
+    mbar_init(&bars->never, 1);
     for (int s = 0; s < L::kStages; ++s) {
       mbar_init(&bars->kv_full[s], 1);
       mbar_init(&bars->kv_empty[s], 1);
@@ -305,7 +308,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       bool ok = true;
       int it = 0;
-      if (n_kv > 0) ok = mbar_wait_bounded(&bars->q_full, 0, abort_flag, kTimeoutNs);
+      // Self-test of the failure path: wait on a barrier nothing arrives on, so the wait
+      // runs out, the kernel records the timeout and every role returns.
+      if (p.selftest_stall) ok = mbar_wait_bounded(&bars->never, 0, abort_flag, kTimeoutNs);
+      if (ok && n_kv > 0) ok = mbar_wait_bounded(&bars->q_full, 0, abort_flag, kTimeoutNs);
       if (ok && n_kv > 0) {
         const int st = 0;
         ok = mbar_wait_bounded(&bars->kv_full[st], 0, abort_flag, kTimeoutNs);

@@ -18,6 +18,8 @@ struct FwdParams {
   int64_t o_split_stride;  // output element stride between slices (partial mode)
   float scale_log2;        // scale * log2(e)
   unsigned long long* trace;  // experiment builds (-DTA_TRACE) only: event clocks
+  unsigned long long timeout_ns;  // limit of every in-kernel wait (0: 1 s)
+  int selftest_stall;      // 1: the MMA warp waits on a barrier nothing arrives on
 };
 
 // Query rows one CTA covers (two 128-row tiles).
