@@ -22,7 +22,9 @@
  * Layout: q, k, v, o are 4-D [B, H, S, D] tensors given by a base pointer and four
  * element strides (batch, head, sequence, dim). The dim stride must be 1; the other
  * strides times the element size must be multiples of 16 bytes and the base pointers
- * 16-byte aligned (TMA descriptor rules). Supported head dims: 64, 128.
+ * 16-byte aligned (TMA descriptor rules). Supported head dims: 64, 128, 256 (other head
+ * dims are zero-padded to the next one by the Python launcher, as the reference pads to
+ * the next power of two, flash_fwd.py:149-163).
  */
 #ifndef TILEDATTENTION_B200_H
 #define TILEDATTENTION_B200_H
@@ -36,7 +38,7 @@ extern "C" {
 /* Status codes. */
 #define TA_OK                   0
 #define TA_ERR_INVALID_ARGUMENT 1  /* null pointer, non-positive size, bad scale      */
-#define TA_ERR_UNSUPPORTED_DIM  2  /* head dim not in {64, 128}                       */
+#define TA_ERR_UNSUPPORTED_DIM  2  /* head dim not in {64, 128, 256}                  */
 #define TA_ERR_UNSUPPORTED_DTYPE 3 /* dtype not TA_DTYPE_F16 / TA_DTYPE_BF16          */
 #define TA_ERR_LAYOUT           4  /* stride / alignment not expressible as a TMA map */
 #define TA_ERR_CUDA             5  /* a CUDA runtime call failed (see ta_last_error)  */

@@ -202,6 +202,7 @@ def test_valid_input_reaches_launcher(fake_runtime, monkeypatch):
 def test_padded_head_dim_policy():
     from tiledattention_b200.launch import padded_head_dim
 
-    assert [padded_head_dim(d) for d in (1, 32, 64, 65, 96, 128)] == [64, 64, 64, 128, 128, 128]
+    assert [padded_head_dim(d) for d in (1, 32, 64, 65, 96, 128, 129, 160, 256)] == [
+        64, 64, 64, 128, 128, 128, 256, 256, 256]
     with pytest.raises(InvalidShapeError):
-        padded_head_dim(160)
+        padded_head_dim(257)

@@ -112,7 +112,15 @@ def test_strided_bshd_layout():
     _check(q, k, v, True)
 
 
-@pytest.mark.parametrize("D", [32, 80, 96])
+@pytest.mark.parametrize("D", [32, 80, 96, 160, 192])
 def test_padded_head_dims(D):
     q, k, v = _inputs(1, 2, 200, D, torch.float16, D)
     _check(q, k, v, False)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("S", [300, 1024])
+def test_head_dim_256(S, causal, dtype):
+    q, k, v = _inputs(1, 3, S, 256, dtype, S + 256)
+    _check(q, k, v, causal)

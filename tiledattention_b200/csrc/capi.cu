@@ -136,7 +136,7 @@ const char* ta_status_string(int status) {
   switch (status) {
     case TA_OK: return "ok";
     case TA_ERR_INVALID_ARGUMENT: return "invalid argument";
-    case TA_ERR_UNSUPPORTED_DIM: return "unsupported head dim (supported: 64, 128)";
+    case TA_ERR_UNSUPPORTED_DIM: return "unsupported head dim (supported: 64, 128, 256)";
     case TA_ERR_UNSUPPORTED_DTYPE: return "unsupported dtype (supported: float16, bfloat16)";
     case TA_ERR_LAYOUT: return "layout not expressible as a TMA tensor map";
     case TA_ERR_CUDA: return "CUDA runtime error";
@@ -168,7 +168,8 @@ int run_forward(const void* q, const void* k, const void* v, void* o, bool out_f
     return fail(TA_ERR_INVALID_ARGUMENT, "null pointer argument");
   if (B <= 0 || H <= 0 || S <= 0)
     return fail(TA_ERR_INVALID_ARGUMENT, "B, H, S must be positive (got %d, %d, %d)", B, H, S);
-  if (D != 64 && D != 128) return fail(TA_ERR_UNSUPPORTED_DIM, "head dim %d not in {64, 128}", D);
+  if (D != 64 && D != 128 && D != 256)
+    return fail(TA_ERR_UNSUPPORTED_DIM, "head dim %d not in {64, 128, 256}", D);
   if (dtype != TA_DTYPE_F16 && dtype != TA_DTYPE_BF16)
     return fail(TA_ERR_UNSUPPORTED_DTYPE, "dtype code %d", dtype);
   if (!(scale > 0.f) || !std::isfinite(scale))
@@ -210,7 +211,7 @@ int run_forward(const void* q, const void* k, const void* v, void* o, bool out_f
   const int span = kv_end - kv_begin;
   p.split_len = ((span + n_split - 1) / n_split + 127) / 128 * 128;
   if (p.split_len == 0) p.split_len = 128;
-  p.n_qblk = (S + ta::rows_per_cta() - 1) / ta::rows_per_cta();
+  p.n_qblk = (S + ta::rows_per_cta(D) - 1) / ta::rows_per_cta(D);
   p.scale_log2 = static_cast<float>(static_cast<double>(scale) * 1.4426950408889634);
 #ifdef TA_TRACE
   p.trace = g_trace;
@@ -256,7 +257,8 @@ int ta_lse_combine(const float* o_part, const float* lse_part, int n_split, int 
     return fail(TA_ERR_INVALID_ARGUMENT, "null pointer argument");
   if (B <= 0 || H <= 0 || S <= 0 || n_split < 1)
     return fail(TA_ERR_INVALID_ARGUMENT, "B, H, S, n_split must be positive");
-  if (D != 64 && D != 128) return fail(TA_ERR_UNSUPPORTED_DIM, "head dim %d not in {64, 128}", D);
+  if (D != 64 && D != 128 && D != 256)
+    return fail(TA_ERR_UNSUPPORTED_DIM, "head dim %d not in {64, 128, 256}", D);
   if (out_dtype != TA_DTYPE_F16 && out_dtype != TA_DTYPE_BF16 && out_dtype != TA_DTYPE_F32)
     return fail(TA_ERR_UNSUPPORTED_DTYPE, "output dtype code %d", out_dtype);
   const int64_t esz = out_dtype == TA_DTYPE_F32 ? 4 : 2;

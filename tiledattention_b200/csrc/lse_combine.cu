@@ -78,6 +78,7 @@ cudaError_t launch_lse_combine(const CombineParams& p, int D, int out_kind, cuda
 #define TA_COMB(DD, OO) \
   if (D == DD && out_kind == OO) { lse_combine_kernel<DD, OO><<<static_cast<int>(grid), 256, 0, stream>>>(p); return cudaGetLastError(); }
   TA_COMB(64, 0) TA_COMB(64, 1) TA_COMB(64, 2) TA_COMB(128, 0) TA_COMB(128, 1) TA_COMB(128, 2)
+  TA_COMB(256, 0) TA_COMB(256, 1) TA_COMB(256, 2)
 #undef TA_COMB
   return cudaErrorInvalidValue;
 }

@@ -47,8 +47,10 @@
 namespace ta {
 
 constexpr int kRowsPerTile = 128;  // query rows per tile (= TMEM lanes)
-constexpr int kTilesPerCta = 2;    // query tiles per CTA
-constexpr int kRowsPerCta = kRowsPerTile * kTilesPerCta;
+// Query tiles per CTA: two 128-row tiles up to D=128; one at D=256, where S (128) + O (256)
+// tensor-memory columns per tile leave no room for a second tile.
+template <int D>
+constexpr int tiles_per_cta() { return D == 256 ? 1 : 2; }
 constexpr int kKeysPerTile = 128;  // keys per K/V tile
 constexpr int kThreads = 384;
 // Register split: the kernel is built for kLaunchRegs per thread (launch bounds 384 x 1);
@@ -95,9 +97,11 @@ template <int D>
 struct Layout {
   static constexpr int kTileBytes = kRowsPerTile * D * 2;  // 128 rows x D x 16-bit
   static constexpr int kChunks = D / 64;                   // 128-byte swizzle atoms per row
-  static constexpr int kStages = (D == 64) ? 6 : 4;
+  static constexpr int kTiles = tiles_per_cta<D>();
+  static constexpr int kRowsPerCta = kRowsPerTile * kTiles;
+  static constexpr int kStages = (D == 64) ? 6 : (D == 128 ? 4 : 2);
   static constexpr int kQOff = 0;
-  static constexpr int kKVOff = kQOff + kTilesPerCta * kTileBytes;
+  static constexpr int kKVOff = kQOff + kTiles * kTileBytes;
   static constexpr int kBarOff = kKVOff + kStages * kTileBytes;
   static constexpr int kBytes = kBarOff + 256;
   static constexpr int kDynSmem = kBytes + 1024;  // slack for 1024-byte alignment
@@ -205,8 +209,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   // keys [kv_lo, kv_hi) take part (the whole range, or one slice for split-KV)
   const int kv_lo = min(p.kv_end, p.kv_begin + split * p.split_len);
   const int kv_hi = min(p.kv_end, kv_lo + p.split_len);
-  const int q_row0 = qblk * kRowsPerCta;
-  const int kv_rows = CAUSAL ? min(kv_hi, q_row0 + kRowsPerCta) : kv_hi;
+  const int q_row0 = qblk * L::kRowsPerCta;
+  const int kv_rows = CAUSAL ? min(kv_hi, q_row0 + L::kRowsPerCta) : kv_hi;
   const int n_kv = kv_rows > kv_lo ? (kv_rows - kv_lo + kKeysPerTile - 1) / kKeysPerTile : 0;
 
   if (threadIdx.x == 0) {
@@ -246,8 +250,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == kProducerWarp) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      mbar_arrive_expect_tx(&bars->q_full, kTilesPerCta * L::kTileBytes);
-      for (int t = 0; t < kTilesPerCta; ++t)
+      mbar_arrive_expect_tx(&bars->q_full, L::kTiles * L::kTileBytes);
+      for (int t = 0; t < L::kTiles; ++t)
         for (int c = 0; c < L::kChunks; ++c)
           tma_load_4d(q_smem + t * L::kTileBytes + c * (kRowsPerTile * 128), &tmap_q,
                       &bars->q_full, c * 64, q_row0 + t * kRowsPerTile, h, b);
@@ -319,8 +323,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           issue_qk(0, st);
           mma_commit(&bars->s_full[0]);
-          issue_qk(1, st);
-          mma_commit(&bars->s_full[1]);
+          if constexpr (L::kTiles == 2) {
+            issue_qk(1, st);
+            mma_commit(&bars->s_full[1]);
+          }
           mma_commit(&bars->kv_empty[st]);
           it = 1;
         }
@@ -348,21 +354,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else {
           mma_commit(&bars->o_final[0]);
         }
-        // query tile 1
-        TRACE(j, 9);
-        ok = MMA_WAIT(&bars->p_full[1], j & 1, abort_flag, kTimeoutNs);
-        if (!ok) break;
-        TRACE(j, 10);
-        tc_fence_after();
-        issue_pv(1, st_v, j > 0);
-        mma_commit(&bars->kv_empty[st_v]);
-        if (more) {
-          issue_qk(1, st_k);
-          mma_commit(&bars->s_full[1]);
-          mma_commit(&bars->kv_empty[st_k]);
-          ++it;
+        if constexpr (L::kTiles == 2) {
+          // query tile 1
+          TRACE(j, 9);
+          ok = MMA_WAIT(&bars->p_full[1], j & 1, abort_flag, kTimeoutNs);
+          if (!ok) break;
+          TRACE(j, 10);
+          tc_fence_after();
+          issue_pv(1, st_v, j > 0);
+          mma_commit(&bars->kv_empty[st_v]);
+          if (more) {
+            issue_qk(1, st_k);
+            mma_commit(&bars->s_full[1]);
+            mma_commit(&bars->kv_empty[st_k]);
+            ++it;
+          } else {
+            mma_commit(&bars->o_final[1]);
+          }
         } else {
-          mma_commit(&bars->o_final[1]);
+          mma_commit(&bars->kv_empty[st_v]);
+          if (more) {
+            mma_commit(&bars->kv_empty[st_k]);
+            ++it;
+          }
         }
         TRACE(j, 11);
       }
@@ -379,6 +393,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     regs_inc<kSoftmaxRegs>();
     // ------------------------------------------------------------ softmax + epilogue
     const int t = warp >> 2;            // query tile of this warpgroup
+    if (t < L::kTiles) {
     const int quarter = warp & 3;       // TMEM lane quarter this warp may access
     const int r_in_tile = quarter * 32 + lane;
     const int tile_row0 = q_row0 + t * kRowsPerTile;
@@ -594,6 +609,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               l_run > 0.f ? (m_run + __log2f(l_run)) * 0.69314718055994531f : -INFINITY;
       }
     }
+    }  // t < kTiles
   }
 
   tc_fence_before();
@@ -644,11 +660,17 @@ cudaError_t launch_sdpa_fwd(const CUtensorMap& q, const CUtensorMap& k, const CU
   TA_DISPATCH2(128, false, true)
   TA_DISPATCH2(128, true, false)
   TA_DISPATCH2(128, true, true)
+  TA_DISPATCH2(256, false, false)
+  TA_DISPATCH2(256, false, true)
+  TA_DISPATCH2(256, true, false)
+  TA_DISPATCH2(256, true, true)
 #undef TA_DISPATCH2
 #undef TA_DISPATCH
   return cudaErrorInvalidValue;
 }
 
-int rows_per_cta() { return kRowsPerCta; }
+int rows_per_cta(int D) {
+  return D == 256 ? Layout<256>::kRowsPerCta : (D == 128 ? Layout<128>::kRowsPerCta : Layout<64>::kRowsPerCta);
+}
 
 }  // namespace ta

@@ -22,8 +22,8 @@ struct FwdParams {
   int selftest_stall;      // 1: the MMA warp waits on a barrier nothing arrives on
 };
 
-// Query rows one CTA covers (two 128-row tiles).
-int rows_per_cta();
+// Query rows one CTA covers for head dim D (two 128-row tiles; one at D=256).
+int rows_per_cta(int D);
 
 // Launches the variant for (D, dtype, causal) on `stream`. Tensor maps are 4-D
 // (D, S, H, B) with a 64 x 128 box and 128-byte swizzle.

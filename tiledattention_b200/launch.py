@@ -6,7 +6,7 @@ _launch_cutile_kernel (flash_fwd.py:786-818) of the reference:
     ABI turns into TMA tensor maps; only layouts TMA cannot express (head-dim stride
     != 1, strides or base not 16-byte aligned) are made contiguous first, as the
     reference does unconditionally (flash_fwd.py:865-867);
-  * head dims other than 64/128 are zero-padded to the next supported size
+  * head dims other than 64/128/256 are zero-padded to the next supported size
     (flash_fwd.py:149-163, 868-872); the scale is resolved by the caller from the
     original head dim (sdpa.py:46-47), so padding does not change the result;
   * the output is a fresh tensor like empty_like(q) (flash_fwd.py:877);
@@ -29,7 +29,7 @@ from ._errors import (
     UnsupportedPlatformError,
 )
 
-NATIVE_HEAD_DIMS = (64, 128)
+NATIVE_HEAD_DIMS = (64, 128, 256)
 _status_words: dict[int, object] = {}
 
 
@@ -39,7 +39,7 @@ def padded_head_dim(head_dim: int) -> int:
         if head_dim <= d:
             return d
     raise InvalidShapeError(
-        f"head dim {head_dim} is not supported (this build supports head dims up to 128)."
+        f"head dim {head_dim} is not supported (this build supports head dims up to 256)."
     )
 
 
