@@ -41,12 +41,13 @@ DEVSTAT_BITS = {
 # Every symbol include/tiledattention_b200.h declares, with its ctypes signature.
 _I64P = ctypes.POINTER(ctypes.c_int64)
 SIGNATURES = {
+    # stride arguments as plain addresses (ctypes arrays or ints), for a cheap hot call
     "ta_sdpa_fwd": (
         ctypes.c_int,
         [
             ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
             ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
-            _I64P, _I64P, _I64P, _I64P,
+            ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
             ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p,
         ],
     ),
@@ -128,6 +129,18 @@ def status_string(lib: ctypes.CDLL, code: int) -> str:
 def strides4(strides) -> ctypes.Array:
     arr = (ctypes.c_int64 * 4)(*[int(s) for s in strides])
     return arr
+
+
+_I64x16 = ctypes.c_int64 * 16
+_I64_SIZE = ctypes.sizeof(ctypes.c_int64)
+
+
+def strides16(*stride_tuples):
+    """Four 4-element stride tuples packed in one ctypes array; returns the addresses of
+    its four sub-arrays and the array itself (keep the tuple alive during the call)."""
+    arr = _I64x16(*[int(x) for t in stride_tuples for x in t])
+    base = ctypes.addressof(arr)
+    return (base, base + 4 * _I64_SIZE, base + 8 * _I64_SIZE, base + 12 * _I64_SIZE, arr)
 
 
 def describe_devstat(word: int) -> str:

@@ -67,6 +67,8 @@ def _query_compute_capability(torch_mod: ModuleType) -> tuple[int, int]:
 def require_supported_runtime() -> None:
     """Raise UnsupportedPlatformError / DependencyError unless a B200 and the library exist."""
     global _runtime_ready
+    if _runtime_ready:  # fast path; the lock below guards the one-time initialisation
+        return
     with _runtime_lock:
         if _runtime_ready:
             return

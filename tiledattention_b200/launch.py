@@ -19,6 +19,7 @@ _launch_cutile_kernel (flash_fwd.py:786-818) of the reference:
 
 from __future__ import annotations
 
+import contextlib
 import os
 
 from . import _native, _runtime
@@ -30,6 +31,15 @@ from ._errors import (
 )
 
 NATIVE_HEAD_DIMS = (64, 128, 256)
+_NULL_CTX = contextlib.nullcontext()
+
+
+def _raw_stream(torch_mod, dev_idx: int) -> int:
+    """cudaStream_t of torch's current stream on device dev_idx (fast path when available)."""
+    raw = getattr(torch_mod._C, "_cuda_getCurrentRawStream", None)
+    if raw is not None:
+        return raw(dev_idx)
+    return torch_mod.cuda.current_stream(dev_idx).cuda_stream
 _status_words: dict[int, object] = {}
 
 
@@ -66,6 +76,8 @@ def check_device_status(device=None) -> None:
 
 
 def _tma_compatible(t) -> bool:
+    if t.is_contiguous():  # [B,H,S,D] contiguous: strides are multiples of D (16-bit, D >= 64)
+        return t.data_ptr() % 16 == 0
     if t.stride(-1) != 1 or t.data_ptr() % 16:
         return False
     for dim in range(3):
@@ -111,39 +123,32 @@ def run_sdpa_fwd(q, k, v, *, causal: bool, scale: float, return_lse: bool = Fals
     q, k, v = (t if _tma_compatible(t) else t.contiguous() for t in (q, k, v))
 
     mode = _sync_mode()
-    with torch_mod.cuda.device(q.device):
+    dev_idx = q.device.index if q.device.index is not None else torch_mod.cuda.current_device()
+    switch = dev_idx != torch_mod.cuda.current_device()
+    ctx = torch_mod.cuda.device(dev_idx) if switch else _NULL_CTX
+    with ctx:
         status = _status_word(torch_mod, q.device)
-        stream = torch_mod.cuda.current_stream(q.device).cuda_stream
+        stream = _raw_stream(torch_mod, dev_idx)
         if mode == "strict":
             torch_mod.cuda.synchronize(q.device)
+        st = _native.strides16(q.stride(), k.stride(), v.stride(), out.stride())
         rc = lib.ta_sdpa_fwd(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
             lse.data_ptr() if lse is not None else None,
-            batch, heads, seq_len, kdim,
-            _native.strides4(q.stride()), _native.strides4(k.stride()),
-            _native.strides4(v.stride()), _native.strides4(out.stride()),
+            batch, heads, seq_len, kdim, st[0], st[1], st[2], st[3],
             dtype_code, 1 if causal else 0, float(scale), status.data_ptr(), stream,
         )
         if rc == _native.TA_ERR_LAYOUT and not all(t.is_contiguous() for t in (q, k, v)):
             q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+            st = _native.strides16(q.stride(), k.stride(), v.stride(), out.stride())
             rc = lib.ta_sdpa_fwd(
                 q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
                 lse.data_ptr() if lse is not None else None,
-                batch, heads, seq_len, kdim,
-                _native.strides4(q.stride()), _native.strides4(k.stride()),
-                _native.strides4(v.stride()), _native.strides4(out.stride()),
+                batch, heads, seq_len, kdim, st[0], st[1], st[2], st[3],
                 dtype_code, 1 if causal else 0, float(scale), status.data_ptr(), stream,
             )
         if rc != _native.TA_OK:
-            detail = _native.last_error(lib) or _native.status_string(lib, rc)
-            if rc == _native.TA_ERR_DEVICE:
-                raise UnsupportedPlatformError(detail)
-            if rc in (_native.TA_ERR_INVALID_ARGUMENT, _native.TA_ERR_UNSUPPORTED_DIM,
-                      _native.TA_ERR_LAYOUT):
-                raise InvalidShapeError(detail)
-            if rc == _native.TA_ERR_UNSUPPORTED_DTYPE:
-                raise DTypeNotSupportedError(detail)
-            raise KernelError(detail)
+            _raise_for(lib, rc)
         if mode in ("post", "strict"):
             check_device_status(q.device)
 
