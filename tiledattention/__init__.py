@@ -15,6 +15,8 @@ from tiledattention_b200 import (  # noqa: F401
     UnsupportedPlatformError,
     __version__,
     check_device_status,
+    sdpa_partial,
+    sdpa_split_kv,
     sdpa_with_lse,
 )
 

@@ -72,21 +72,8 @@ constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;      // log2 units
-#ifndef TA_ROWSUM
-#define TA_ROWSUM 1  // 0: unpack + packed add, 1: mixed-precision add, 2: unrounded p
-#endif
-#ifdef TA_MMA_SPIN
-#define MMA_WAIT mbar_spin_bounded
-#else
 #define MMA_WAIT mbar_wait_bounded
-#endif
-#ifndef TA_ABL
-#define TA_ABL 0  // experiment switches (0 in the product build)
-#endif
-#ifndef TA_SUM_CHAINS
-#define TA_SUM_CHAINS 4
-#endif
-constexpr int kSumChains = TA_SUM_CHAINS;
+constexpr int kSumChains = 4;  // independent row-sum accumulators (short dependency chains)
 #ifndef TA_POLY_EVERY
 #define TA_POLY_EVERY 0
 #endif
@@ -150,16 +137,6 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   else
     asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
-}
-
-template <bool BF16>
-__device__ __forceinline__ float2 unpack2(uint32_t w) {
-  if constexpr (BF16) {
-    return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
-  } else {
-    __half2 h = *reinterpret_cast<__half2*>(&w);
-    return __half22float2(h);
-  }
 }
 
 // acc_lo += low 16-bit value of w, acc_hi += high one (fp32 accumulation of bf16/fp16).
@@ -412,11 +389,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
       tc_fence_after();
       if (threadIdx.x % 128 == 0) TRACE(j, 0 + 4 * t);
-#if TA_ABL & 8
-      tc_fence_before();
-      mbar_arrive(&bars->p_full[t]);
-      continue;
-#endif
       float s[kKeysPerTile];
       {
         uint32_t r0[32], r1[32], r2[32], r3[32];
@@ -484,15 +456,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      // p = 2^(s*scale*log2e - m): packed FMA, then exp2 on the MUFU for most pairs and
-      // on the FMA pipe (polynomial) for every kPolyEvery-th pair, to balance the pipes.
+      // p = 2^(s*scale*log2e - m): packed FMA, then exp2 on the MUFU (or, with
+      // TA_POLY_EVERY > 0, every kPolyEvery-th pair on the FMA pipe).
       if (threadIdx.x % 128 == 0) TRACE(j, 2 + 4 * t);
       // A row with no valid key yet (m = -inf; only possible with a key slice) uses 0 as
       // the subtrahend, so its weights are exactly 0 instead of NaN.
       const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
       const uint64_t sl2 = f2_pack(sl, sl);
       const uint64_t negm2 = f2_pack(-m_use, -m_use);
-      // Row sum in kSumChains independent fp32 accumulator pairs (short dependency chains).
       float acc_lo[kSumChains], acc_hi[kSumChains];
 #pragma unroll
       for (int c = 0; c < kSumChains; ++c) acc_lo[c] = acc_hi[c] = 0.f;
@@ -503,41 +474,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 32; ++i) {
           const int e = 64 * half + 2 * i;
           float p0, p1;
-#if TA_ABL & 2
-          const float x0 = fmaf(s[e], sl, -m_run), x1 = fmaf(s[e + 1], sl, -m_run);
-          p0 = ex2_approx(x0);
-          p1 = ex2_approx(x1);
-#else
           const uint64_t x2 = f2_fma(f2_pack(s[e], s[e + 1]), sl2, negm2);
           if (kPolyEvery > 0 && (i % (kPolyEvery > 0 ? kPolyEvery : 1)) == kPolyEvery - 1) {
             f2_unpack(exp2_poly_x2(x2), p0, p1);
           } else {
             float x0, x1;
             f2_unpack(x2, x0, x1);
-#if TA_ABL & 4
-            p0 = x0; p1 = x1;
-#else
             p0 = ex2_approx(x0);
             p1 = ex2_approx(x1);
-#endif
           }
-#endif
           pk[i] = pack2<BF16>(p0, p1);
-#if TA_ABL & 1
-#elif TA_ROWSUM == 0
-          // The row sum uses the rounded weights the P.V MMA sees, so the output is
-          // an exact convex combination of V rows with those weights.
-          {
-            const float2 r = unpack2<BF16>(pk[i]);
-            acc_lo[i % kSumChains] += r.x;
-            acc_hi[i % kSumChains] += r.y;
-          }
-#elif TA_ROWSUM == 1
+          // The row sum uses the rounded weights the P.V MMA sees, so the output is an
+          // exact convex combination of V rows with those weights.
           add_packed16_to_f32<BF16>(pk[i], acc_lo[i % kSumChains], acc_hi[i % kSumChains]);
-#else
-          acc_lo[i % kSumChains] += p0;
-          acc_hi[i % kSumChains] += p1;
-#endif
         }
         tmem_st32(t_s + 32 * half, pk);
       }
