@@ -410,6 +410,8 @@ def main():
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak,
                      "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
                      "peak_source": f"{peak_kind} bf16_tflops (burst)",
+                     "frac_of_sustained_peak": round(
+                         achieved / float(peaks.get("bf16_tflops_sustained", peak)), 4),
                      "traffic": traffic},
         "cpu_baseline": cpu,
         "clocks": clocks,
