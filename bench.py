@@ -181,7 +181,10 @@ def run_reference_arm(args, rank, world):
     if rank != 0:
         return
     wl = WORKLOAD
-    per_step = max(0.5, float(os.environ.get("TA_REF_STEP_S", "2.0")))
+    # Each step is a bounded sample; its length shrinks with the step count so that the
+    # whole --steps K --warmup W run stays within about two minutes.
+    default_step = min(2.0, max(0.2, 120.0 / (args.steps + 0.25 * args.warmup)))
+    per_step = max(0.1, float(os.environ.get("TA_REF_STEP_S", str(default_step))))
     for _ in range(args.warmup):
         cpu_sample(wl["S"], wl["D"], wl["causal"], per_step / 4)
     vals, descs, total = [], [], 0.0
