@@ -236,6 +236,10 @@ def main():
                     help="bh: shard (batch, head) pairs over ranks, no collective; split_kv: "
                          "every rank takes zig-zag key slices of all pairs, NCCL log-sum-exp "
                          "merge inside the timed step (n_split=4 slices on one GPU)")
+    ap.add_argument("--exchange", choices=["collective", "peer"], default="peer",
+                    help="split_kv at N>1: merge the ranks' states with NCCL all-reduces "
+                         "(collective) or over NVLink peer memory with this package's barrier "
+                         "and merge kernels (peer)")
     ap.add_argument("--pairs", type=int, default=0,
                     help="profiling case: run only this many of the 256 (b,h) pairs")
     args = ap.parse_args()
@@ -270,7 +274,8 @@ def main():
             from tiledattention_b200.distributed import sdpa_split_kv_distributed
 
             def step_fn(q_, k_, v_):
-                return sdpa_split_kv_distributed(q_, k_, v_, causal=causal)[0]
+                return sdpa_split_kv_distributed(q_, k_, v_, causal=causal,
+                                                 exchange=args.exchange)[0]
         else:
             def step_fn(q_, k_, v_):
                 return ta.sdpa_split_kv(q_, k_, v_, causal=causal, n_split=4)
@@ -404,6 +409,7 @@ def main():
                    "B": B, "H": H, "S": S, "D": D, "causal": causal,
                    "pairs_per_gpu": pairs,
                    "parallelism": (f"bh-shard{world}" if args.mode == "bh" else f"split-kv{world}"),
+                   **({"exchange": args.exchange} if args.mode == "split_kv" and world > 1 else {}),
                    "l2": "256 MB L2 flush enqueued before every timed step",
                    "pct_of_bf16_peak": round(100 * value / world / peak, 2)},
         "e2e": {"value": round(e2e_value, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
@@ -418,7 +424,10 @@ def main():
                      "traffic": traffic},
         "cpu_baseline": cpu,
         "clocks": clocks,
-        "gpu_launches": args.steps * world * (1 if args.mode == "bh" else (3 if world > 1 else 2)),
+        # per rank and step: bh 1 forward; split_kv on one GPU forward + combine; at N>1 two
+        # zig-zag partial forwards + combine (collective) or + barrier, merge, barrier (peer)
+        "gpu_launches": args.steps * world * (
+            1 if args.mode == "bh" else (2 if world == 1 else (5 if args.exchange == "peer" else 3))),
     }
     print(json.dumps(line), flush=True)
     if world > 1:

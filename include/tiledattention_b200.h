@@ -58,6 +58,10 @@ extern "C" {
 #define TA_DEVSTAT_TIMEOUT_SOFTMAX 4u
 #define TA_DEVSTAT_TIMEOUT_EPILOG  8u
 #define TA_DEVSTAT_TIMEOUT_DRAIN   16u
+#define TA_DEVSTAT_PEER_TIMEOUT    32u  /* ta_peer_barrier: a peer did not arrive in time */
+
+/* Largest group ta_peer_barrier / ta_lse_merge_peers serve (one NVLink domain of 8 GPUs). */
+#define TA_MAX_PEERS 8
 
 /*
  * ta_sdpa_fwd — o = softmax(q k^T * scale + mask) v, one launch, asynchronous on `stream`.
@@ -115,6 +119,39 @@ int ta_sdpa_fwd_partial(const void* q, const void* k, const void* v, float* o_pa
 int ta_lse_combine(const float* o_part, const float* lse_part, int n_split,
                    int B, int H, int S, int D, void* o, const int64_t* o_strides,
                    int out_dtype, float* lse, void* stream);
+
+/*
+ * Multi-GPU split-KV exchange over peer memory (no reference counterpart: the reference is
+ * single-GPU). Each GPU of a group of n <= TA_MAX_PEERS leaves its split-KV state in memory
+ * every peer has mapped (torch symmetric memory, CUDA IPC); the device addresses passed here
+ * are this process's mappings of the peers' buffers.
+ *
+ * ta_peer_barrier — one-CTA device barrier on `stream`: stores `epoch` into
+ * flags[i][rank] for every peer i (release, system scope) and waits until flags[rank][i]
+ * reached `epoch` for every i (acquire, system scope; wrap-around safe). flags[i] is peer
+ * i's array of TA_MAX_PEERS uint32 words, zeroed before first use; epochs increase by one per
+ * barrier and every rank passes the same sequence. A wait that exceeds timeout_ns (0: 1 s)
+ * sets TA_DEVSTAT_PEER_TIMEOUT in *dev_status (if given) and the kernel returns.
+ */
+int ta_peer_barrier(unsigned int* const* flags, int n_peers, int rank, unsigned int epoch,
+                    unsigned long long timeout_ns, unsigned int* dev_status, void* stream);
+
+/*
+ * ta_lse_merge_peers — log-sum-exp merge of n_src <= 16 split-KV states read directly from
+ * the peers' memory: o_src[i] fp32 [B*H][S][D] and lse_src[i] fp32 [B*H*S] (natural log,
+ * -inf for a slice without keys; D 64, 128 or 256). Rows s in [s_begin, s_end) of every
+ * (b,h) are merged and written to each of the n_dst <= TA_MAX_PEERS outputs o_dst[j] (dtype
+ * TA_DTYPE_F16 / BF16 / F32, element strides o_strides with unit last stride, row s at
+ * b*o_strides[0] + h*o_strides[1] + (s - row_base)*o_strides[2]) and, where lse_dst[j] is
+ * not null (lse_dst may be null), lse_dst[j][(b*H + h)*out_rows + s - row_base]. One
+ * destination (this GPU) is a reduce-scatter by rows; every peer's output as destinations
+ * fuses the all-gather. The caller orders the call after a ta_peer_barrier that follows all
+ * state writes; if dev_status carries TA_DEVSTAT_PEER_TIMEOUT, NaN is written instead.
+ */
+int ta_lse_merge_peers(const void* const* o_src, const void* const* lse_src, int n_src, int B,
+                       int H, int S, int D, int s_begin, int s_end, void* const* o_dst,
+                       float* const* lse_dst, int n_dst, const int64_t* o_strides, int out_rows,
+                       int row_base, int out_dtype, const unsigned int* dev_status, void* stream);
 
 /*
  * ta_sdpa_fwd_split_noalloc — the split-KV forward (ta_sdpa_fwd_partial over all keys in

@@ -28,6 +28,7 @@ TA_ERR_DEVICE = 7
 
 TA_DTYPE_F16 = 0
 TA_DTYPE_BF16 = 1
+TA_MAX_PEERS = 8
 TA_DTYPE_F32 = 2
 
 DEVSTAT_BITS = {
@@ -36,6 +37,7 @@ DEVSTAT_BITS = {
     4: "softmax wait timed out",
     8: "epilogue wait timed out",
     16: "drain of in-flight copies/MMAs timed out",
+    32: "peer barrier timed out (a peer GPU did not arrive)",
 }
 
 # Every symbol include/tiledattention_b200.h declares, with its ctypes signature.
@@ -67,6 +69,20 @@ SIGNATURES = {
             ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
             ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
             ctypes.c_void_p, _I64P, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
+        ],
+    ),
+    "ta_peer_barrier": (
+        ctypes.c_int,
+        [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_uint, ctypes.c_ulonglong,
+         ctypes.c_void_p, ctypes.c_void_p],
+    ),
+    "ta_lse_merge_peers": (
+        ctypes.c_int,
+        [
+            ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+            ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+            ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, _I64P, ctypes.c_int, ctypes.c_int,
+            ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
         ],
     ),
     "ta_sdpa_fwd_split_noalloc": (

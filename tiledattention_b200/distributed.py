@@ -11,13 +11,23 @@ multi-GPU code; both are new):
   lse, local weights w = exp(lse - lse_max), then one all-reduce(SUM) of [w*o | w]
   (``merge_across_ranks``). The merge works on any device / backend (NCCL on GPUs,
   gloo on CPU for tests).
+
+On GPUs the exchange can instead run over NVLink peer memory with this package's own
+kernels (``PeerExchange``): the per-rank states are written into a buffer every rank has
+mapped (torch symmetric memory), a bounded device barrier (ta_peer_barrier) orders them,
+and one merge kernel per rank reads its share of query rows from every peer and writes the
+merged rows — to itself (a reduce-scatter by rows) or to every rank (the all-gather fused
+into the same pass). No collective library is in that data path.
 """
 
 from __future__ import annotations
 
+import ctypes
 import math
+import os
 
 KEY_TILE = 128
+SLICES_PER_RANK = 2  # zig-zag: every rank owns two key ranges
 
 
 def shard_pairs(n_pairs: int, world: int, rank: int) -> tuple[int, int]:
@@ -84,17 +94,191 @@ def merge_across_ranks(o_part, lse_part, group=None):
     return o, lse
 
 
+def row_share(seq_len: int, world: int, rank: int) -> tuple[int, int]:
+    """Query rows [begin, end) whose merge `rank` performs in the peer exchange."""
+    base, extra = divmod(seq_len, world)
+    begin = rank * base + min(rank, extra)
+    return begin, begin + base + (1 if rank < extra else 0)
+
+
+def _align(n: int, a: int = 256) -> int:
+    return (n + a - 1) // a * a
+
+
+class PeerExchange:
+    """Split-KV state exchange over NVLink peer memory for one (shape, dtype, group).
+
+    Holds one symmetric-memory allocation per rank, mapped by every peer, laid out as
+        [flags: TA_MAX_PEERS uint32 | pad to 256 B]
+        2 x [o_state fp32 [2][B*H][S][Dk] | lse_state fp32 [2][B*H*S]
+             | out (dtype) [B*H][S][Dk] | lse_out fp32 [B*H*S]]
+    The two state sets alternate between calls, so a rank never overwrites a state a peer
+    may still be reading (the barrier of the next call orders that). Every rank must call
+    ``forward`` the same number of times, in the same order.
+    """
+
+    def __init__(self, shape, dtype, device, group=None):
+        import torch
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+
+        from . import _native
+
+        self.torch = torch
+        self.group = group if group is not None else dist.group.WORLD
+        self.world = dist.get_world_size(self.group)
+        self.rank = dist.get_rank(self.group)
+        if self.world > _native.TA_MAX_PEERS:
+            raise ValueError(f"peer exchange serves at most {_native.TA_MAX_PEERS} ranks")
+        batch, heads, seq_len, kdim = (int(x) for x in shape)
+        self.shape, self.dtype, self.device = (batch, heads, seq_len, kdim), dtype, device
+        rows = batch * heads * seq_len
+        elem = torch.empty((), dtype=dtype).element_size()
+        self.off = {}
+        cur = 256
+        for st in range(2):
+            for name, nbytes in (("o_state", SLICES_PER_RANK * rows * kdim * 4),
+                                 ("lse_state", SLICES_PER_RANK * rows * 4),
+                                 ("out", rows * kdim * elem), ("lse_out", rows * 4)):
+                self.off[(name, st)] = cur
+                cur = _align(cur + nbytes)
+        self.nbytes = cur
+        try:
+            symm_mem.enable_symm_mem_for_group(self.group.group_name)
+        except Exception:  # newer torch: rendezvous needs no enabling
+            pass
+        self.buf = symm_mem.empty(self.nbytes, dtype=torch.uint8, device=device)
+        self.handle = symm_mem.rendezvous(self.buf, self.group)
+        self.peer_base = [int(p) for p in self.handle.buffer_ptrs]
+        self.buf[:256].zero_()
+        torch.cuda.synchronize(device)
+        dist.barrier(group=self.group)
+        self.epoch = 0
+        self.calls = 0
+        self.timeout_ns = int(float(os.getenv("TILEDATTN_PEER_TIMEOUT_MS", "10000")) * 1e6)
+        self._flag_ptrs = (ctypes.c_void_p * self.world)(*self.peer_base)
+
+    def _view(self, name: str, st: int, dtype, shape):
+        start = self.off[(name, st)]
+        count = math.prod(shape)
+        nbytes = count * self.torch.empty((), dtype=dtype).element_size()
+        return self.buf[start:start + nbytes].view(dtype).view(shape)
+
+    def _barrier(self, lib, status, stream):
+        from .launch import _raise_for
+
+        self.epoch = (self.epoch + 1) & 0xFFFFFFFF
+        rc = lib.ta_peer_barrier(ctypes.addressof(self._flag_ptrs), self.world, self.rank,
+                                 self.epoch, self.timeout_ns, status.data_ptr(), stream)
+        if rc != 0:
+            _raise_for(lib, rc)
+
+    def forward(self, q, k, v, *, causal: bool, scale: float, gather: bool = True):
+        """Split-KV forward of this rank's zig-zag key slices, then the peer exchange.
+
+        gather=True: every rank returns the full o [B,H,S,D] (dtype of q) and lse [B,H,S].
+        gather=False: this rank returns only its merged query rows o [B,H,rows,D] and lse
+        [B,H,rows], plus (begin, end) of those rows (row_share).
+        """
+        from . import _native, _runtime
+        from .launch import _dtype_code, _raise_for, _status_word, run_sdpa_partial
+
+        torch = self.torch
+        lib = _runtime.get_native_library()
+        batch, heads, seq_len, kdim = self.shape
+        head_dim = int(q.shape[-1])
+        st = self.calls % 2
+        self.calls += 1
+        o_state = self._view("o_state", st, torch.float32,
+                             (SLICES_PER_RANK, batch, heads, seq_len, kdim))
+        lse_state = self._view("lse_state", st, torch.float32,
+                               (SLICES_PER_RANK, batch, heads, seq_len))
+        ranges = list(zigzag_key_ranges(seq_len, self.world, self.rank))
+        for j in range(SLICES_PER_RANK):
+            if j < len(ranges):
+                lo, hi = ranges[j]
+                run_sdpa_partial(q, k, v, causal=causal, scale=scale, kv_begin=lo, kv_end=hi,
+                                 out=(o_state[j:j + 1], lse_state[j:j + 1]))
+            else:
+                lse_state[j].fill_(-math.inf)
+        with torch.cuda.device(q.device):
+            stream = torch.cuda.current_stream(q.device).cuda_stream
+            status = _status_word(torch, q.device)
+            self._barrier(lib, status, stream)
+            o_src, l_src = [], []
+            for base in self.peer_base:
+                for j in range(SLICES_PER_RANK):
+                    o_src.append(base + self.off[("o_state", st)] + j * batch * heads * seq_len * kdim * 4)
+                    l_src.append(base + self.off[("lse_state", st)] + j * batch * heads * seq_len * 4)
+            s_begin, s_end = row_share(seq_len, self.world, self.rank)
+            o_src_arr = (ctypes.c_void_p * len(o_src))(*o_src)
+            l_src_arr = (ctypes.c_void_p * len(l_src))(*l_src)
+            code = _dtype_code(torch, q.dtype)
+            if gather:
+                dsts = [b + self.off[("out", st)] for b in self.peer_base]
+                ldsts = [b + self.off[("lse_out", st)] for b in self.peer_base]
+                strides = (heads * seq_len * kdim, seq_len * kdim, kdim, 1)
+                out_rows, row_base = seq_len, 0
+                result = None
+            else:
+                rows = s_end - s_begin
+                result = torch.empty((batch, heads, rows, kdim), dtype=q.dtype, device=q.device)
+                lse_res = torch.empty((batch, heads, rows), dtype=torch.float32, device=q.device)
+                dsts, ldsts = [result.data_ptr()], [lse_res.data_ptr()]
+                strides = tuple(result.stride())
+                out_rows, row_base = rows, s_begin
+            dst_arr = (ctypes.c_void_p * len(dsts))(*dsts)
+            ldst_arr = (ctypes.c_void_p * len(ldsts))(*ldsts)
+            if s_end > s_begin:
+                rc = lib.ta_lse_merge_peers(
+                    ctypes.addressof(o_src_arr), ctypes.addressof(l_src_arr), len(o_src),
+                    batch, heads, seq_len, kdim, s_begin, s_end, ctypes.addressof(dst_arr),
+                    ctypes.addressof(ldst_arr), len(dsts), _native.strides4(strides), out_rows,
+                    row_base, code, status.data_ptr(), stream)
+                if rc != 0:
+                    _raise_for(lib, rc)
+            if not gather:
+                return result[..., :head_dim], lse_res, (s_begin, s_end)
+            self._barrier(lib, status, stream)
+            o = self._view("out", st, q.dtype, (batch, heads, seq_len, kdim))[..., :head_dim].clone()
+            lse = self._view("lse_out", st, torch.float32, (batch, heads, seq_len)).clone()
+        return o, lse
+
+
+_exchanges: dict = {}
+
+
+def peer_exchange_for(q, kdim: int, group=None) -> PeerExchange:
+    """The cached PeerExchange for q's shape / dtype / device and `group`."""
+    key = (tuple(q.shape[:3]), kdim, q.dtype, q.device.index, id(group))
+    ex = _exchanges.get(key)
+    if ex is None:
+        ex = PeerExchange((*q.shape[:3], kdim), q.dtype, q.device, group)
+        _exchanges[key] = ex
+    return ex
+
+
 def sdpa_split_kv_distributed(q, k, v, *, causal: bool = False, scale: float | None = None,
-                              group=None):
+                              group=None, exchange: str = "collective"):
     """Split-KV SDPA across the ranks of `group` (one GPU each): this rank attends all
-    query rows of q to its zig-zag key slices with the sm_100a kernel, merges its slices
-    on the GPU, and the ranks merge their states with merge_across_ranks. Every rank
-    returns the full output (dtype of q) and the fp32 lse."""
+    query rows of q to its zig-zag key slices with the sm_100a kernel, and the ranks merge
+    their states. Every rank returns the full output (dtype of q) and the fp32 lse.
+
+    exchange="collective": the rank merges its slices on the GPU, then merge_across_ranks
+    (all-reduces; any backend). exchange="peer": PeerExchange over NVLink peer memory
+    (CUDA tensors, every rank's GPU reachable by load/store from every other)."""
     import torch
     import torch.distributed as dist
 
-    from .launch import run_lse_combine
-    from .sdpa import sdpa_partial
+    from .launch import padded_head_dim, run_lse_combine
+    from .sdpa import _prepare, sdpa_partial
+
+    if exchange == "peer":
+        resolved = _prepare(q, k, v, causal, scale)
+        ex = peer_exchange_for(q, padded_head_dim(int(q.shape[-1])), group)
+        return ex.forward(q, k, v, causal=causal, scale=resolved, gather=True)
+    if exchange != "collective":
+        raise ValueError("exchange must be 'collective' or 'peer'")
 
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)

@@ -176,13 +176,15 @@ def _raise_for(lib, rc):
 
 
 def run_sdpa_partial(q, k, v, *, causal: bool, scale: float, kv_begin: int = 0,
-                     kv_end: int | None = None, n_split: int = 1):
+                     kv_end: int | None = None, n_split: int = 1, out=None):
     """Split-KV forward over keys [kv_begin, kv_end) cut into n_split slices.
 
     Returns (o_part, lse_part): fp32 [n_split, B, H, S, Dk] (each slice normalised by its
     own row sum) and fp32 [n_split, B, H, S] natural-log log-sum-exp (-inf where a slice
-    has no valid key for the row). Dk is the kernel head dim (64 or 128); padded head
-    dims are sliced off by the caller. Inputs are already validated.
+    has no valid key for the row). Dk is the kernel head dim (64, 128 or 256); padded head
+    dims are sliced off by the caller. Inputs are already validated. ``out`` = (o_part,
+    lse_part): contiguous fp32 tensors of those shapes to write into (e.g. views of a
+    buffer the peers have mapped) instead of new ones.
     """
     torch_mod = _runtime.get_torch_module()
     lib = _runtime.get_native_library()
@@ -190,10 +192,20 @@ def run_sdpa_partial(q, k, v, *, causal: bool, scale: float, kv_begin: int = 0,
     kdim = padded_head_dim(head_dim)
     kv_end = seq_len if kv_end is None else int(kv_end)
     dtype_code = _dtype_code(torch_mod, q.dtype)
-    o_part = torch_mod.empty((n_split, batch, heads, seq_len, kdim), dtype=torch_mod.float32,
-                             device=q.device)
-    lse_part = torch_mod.empty((n_split, batch, heads, seq_len), dtype=torch_mod.float32,
-                               device=q.device)
+    if out is not None:
+        o_part, lse_part = out
+        if (tuple(o_part.shape) != (n_split, batch, heads, seq_len, kdim)
+                or tuple(lse_part.shape) != (n_split, batch, heads, seq_len)
+                or o_part.dtype != torch_mod.float32 or lse_part.dtype != torch_mod.float32
+                or not o_part.is_contiguous() or not lse_part.is_contiguous()
+                or o_part.data_ptr() % 16):
+            raise InvalidShapeError("out: contiguous fp32 [n_split,B,H,S,Dk] and [n_split,B,H,S] "
+                                    "tensors (16-byte aligned) required")
+    else:
+        o_part = torch_mod.empty((n_split, batch, heads, seq_len, kdim), dtype=torch_mod.float32,
+                                 device=q.device)
+        lse_part = torch_mod.empty((n_split, batch, heads, seq_len), dtype=torch_mod.float32,
+                                   device=q.device)
     if o_part.numel() == 0:
         return o_part, lse_part
     if kdim != head_dim:
