@@ -192,6 +192,10 @@ int run_forward(const void* q, const void* k, const void* v, void* o, bool out_f
   if ((rc = make_map(&mq, q, B, H, S, D, q_strides, dtype, "q"))) return rc;
   if ((rc = make_map(&mk, k, B, H, S, D, k_strides, dtype, "k"))) return rc;
   if ((rc = make_map(&mv, v, B, H, S, D, v_strides, dtype, "v"))) return rc;
+  CUtensorMap mo;
+  memset(&mo, 0, sizeof(mo));
+  if (!out_f32 && D != 256 && (rc = make_map(&mo, o, B, H, S, D, o_strides, dtype, "o")))
+    return rc;
 
   ta::FwdParams p{};
   p.o = o;
@@ -218,8 +222,8 @@ int run_forward(const void* q, const void* k, const void* v, void* o, bool out_f
 #endif
   p.timeout_ns = g_timeout_ns.load();
   p.selftest_stall = g_selftest_stall.load();
-  cudaError_t err = ta::launch_sdpa_fwd(mq, mk, mv, p, D, dtype == TA_DTYPE_BF16, causal != 0,
-                                        out_f32, static_cast<cudaStream_t>(stream));
+  cudaError_t err = ta::launch_sdpa_fwd(mq, mk, mv, mo, p, D, dtype == TA_DTYPE_BF16,
+                                        causal != 0, out_f32, static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess)
     return fail(TA_ERR_CUDA, "kernel launch failed: %s", cudaGetErrorString(err));
   return TA_OK;

@@ -20,15 +20,23 @@ struct FwdParams {
   unsigned long long* trace;  // experiment builds (-DTA_TRACE) only: event clocks
   unsigned long long timeout_ns;  // limit of every in-kernel wait (0: 1 s)
   int selftest_stall;      // 1: the MMA warp waits on a barrier nothing arrives on
+  unsigned int* sched;     // {next work item, CTAs finished} of this launch (set by the launcher)
 };
 
-// Query rows one CTA covers for head dim D (two 128-row tiles; one at D=256).
+// Query rows one CTA covers for head dim D.
 int rows_per_cta(int D);
+
+// The head-dim-256 kernel (sdpa_fwd_sm100_d256.cu), reached through launch_sdpa_fwd.
+cudaError_t launch_sdpa_fwd_d256(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
+                                 const FwdParams& p, bool bf16, bool causal, bool out_f32,
+                                 cudaStream_t stream);
+int rows_per_cta_d256();
 
 // Launches the variant for (D, dtype, causal) on `stream`. Tensor maps are 4-D
 // (D, S, H, B) with a 64 x 128 box and 128-byte swizzle.
+// `o` is a map of the output like q's (used for 16-bit output; ignored when out_f32).
 cudaError_t launch_sdpa_fwd(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
-                            const FwdParams& p, int D, bool bf16, bool causal, bool out_f32,
-                            cudaStream_t stream);
+                            const CUtensorMap& o, const FwdParams& p, int D, bool bf16,
+                            bool causal, bool out_f32, cudaStream_t stream);
 
 }  // namespace ta
