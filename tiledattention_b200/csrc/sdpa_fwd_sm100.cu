@@ -831,7 +831,8 @@ std::atomic<int> g_sm_count[kMaxDevices];
 cudaError_t launch_sdpa_fwd(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
                             const CUtensorMap& o, const FwdParams& p_in, int D, bool bf16,
                             bool causal, bool out_f32, cudaStream_t stream) {
-  if (D == 256) return launch_sdpa_fwd_d256(q, k, v, p_in, bf16, causal, out_f32, stream);
+  if (uses_shared_kv(D, p_in.S))
+    return launch_sdpa_fwd_shared_kv(q, k, v, p_in, D, bf16, causal, out_f32, stream);
   const long long items = static_cast<long long>(p_in.n_split) * p_in.BH * p_in.n_qblk;
   if (items == 0) return cudaSuccess;
   if (items > 0x7fffffffll) return cudaErrorInvalidValue;
@@ -870,6 +871,8 @@ cudaError_t launch_sdpa_fwd(const CUtensorMap& q, const CUtensorMap& k, const CU
   return cudaErrorInvalidValue;
 }
 
-int rows_per_cta(int D) { return D == 256 ? rows_per_cta_d256() : kRowsPerTile; }
+int rows_per_cta(int D, int S) {
+  return uses_shared_kv(D, S) ? rows_per_cta_shared_kv(D) : kRowsPerTile;
+}
 
 }  // namespace ta

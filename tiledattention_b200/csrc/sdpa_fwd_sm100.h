@@ -23,14 +23,21 @@ struct FwdParams {
   unsigned int* sched;     // {next work item, CTAs finished} of this launch (set by the launcher)
 };
 
-// Query rows one CTA covers for head dim D.
-int rows_per_cta(int D);
+// Whether (D, S) runs on the shared-K/V kernel (sdpa_fwd_sm100_shared_kv.cu): head dim 256,
+// and head dim 128 from kSharedKvMinSeq keys on, where the persistent one-tile kernel's
+// lower start-up cost no longer outweighs loading each K/V tile once per 128 rows instead
+// of once per 256 (measured crossover between S = 4096 and 16384 on B200).
+constexpr int kSharedKvMinSeq = 16384;
+inline bool uses_shared_kv(int D, int S) { return D == 256 || (D == 128 && S >= kSharedKvMinSeq); }
 
-// The head-dim-256 kernel (sdpa_fwd_sm100_d256.cu), reached through launch_sdpa_fwd.
-cudaError_t launch_sdpa_fwd_d256(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
-                                 const FwdParams& p, bool bf16, bool causal, bool out_f32,
-                                 cudaStream_t stream);
-int rows_per_cta_d256();
+// Query rows one CTA (one work item of the persistent kernel) covers for (D, S).
+int rows_per_cta(int D, int S);
+
+// The shared-K/V kernel, reached through launch_sdpa_fwd.
+cudaError_t launch_sdpa_fwd_shared_kv(const CUtensorMap& q, const CUtensorMap& k,
+                                      const CUtensorMap& v, const FwdParams& p, int D,
+                                      bool bf16, bool causal, bool out_f32, cudaStream_t stream);
+int rows_per_cta_shared_kv(int D);
 
 // Launches the variant for (D, dtype, causal) on `stream`. Tensor maps are 4-D
 // (D, S, H, B) with a 64 x 128 box and 128-byte swizzle.

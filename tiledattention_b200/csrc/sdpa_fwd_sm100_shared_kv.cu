@@ -1,9 +1,11 @@
-// SDPA forward for B200 (sm_100a) at head dim 256 (also the padded target of head dims
-// 129-255): TMA + mbarrier pipeline, tcgen05 MMAs with accumulators in tensor memory,
-// warp-specialised online softmax. At D=256 the accumulator alone takes 256 of the 512
-// tensor-memory columns, so this kernel keeps one accumulator per query tile and one
-// score buffer (the head-dim 64/128 kernel splits every key tile in two halves with their
-// own accumulators, which does not fit here).
+// SDPA forward for B200 (sm_100a) where query tiles share every K/V tile: head dim 256
+// (also the padded target of head dims 129-255) and long head-dim-128 sequences. TMA +
+// mbarrier pipeline, tcgen05 MMAs with accumulators in tensor memory, warp-specialised
+// online softmax. At D=128 one CTA covers two 128-row query tiles (256 rows), so each K/V
+// tile is loaded and written to shared memory once per 256 rows - half the per-SM copy
+// traffic of the persistent one-tile kernel, which matters once sequences are long and the
+// per-CTA start-up cost is amortised. At D=256 the accumulator alone takes 256 of the 512
+// tensor-memory columns, so the CTA keeps one query tile.
 //
 // Algorithm (same maths as the reference cuTile kernel,
 // src/tiledattention/kernels/flash_fwd.py:374-446 of thisistaimur/TiledAttention):
@@ -49,7 +51,7 @@
 #include "tiledattention_b200.h"
 
 namespace ta {
-namespace d256 {
+namespace shared_kv {
 
 constexpr int kRowsPerTile = 128;  // query rows per tile (= TMEM lanes)
 // Query tiles per CTA: two 128-row tiles up to D=128; one at D=256, where S (128) + O (256)
@@ -596,25 +598,32 @@ static cudaError_t launch_variant(const CUtensorMap& q, const CUtensorMap& k, co
   return cudaGetLastError();
 }
 
-}  // namespace d256
+}  // namespace shared_kv
 
-cudaError_t launch_sdpa_fwd_d256(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
-                                 const FwdParams& p, bool bf16, bool causal, bool out_f32,
-                                 cudaStream_t stream) {
+cudaError_t launch_sdpa_fwd_shared_kv(const CUtensorMap& q, const CUtensorMap& k,
+                                      const CUtensorMap& v, const FwdParams& p, int D,
+                                      bool bf16, bool causal, bool out_f32,
+                                      cudaStream_t stream) {
   const long long grid = static_cast<long long>(p.n_split) * p.BH * p.n_qblk;
   if (grid == 0) return cudaSuccess;
   if (grid > 0x7fffffffll) return cudaErrorInvalidValue;
-#define TA_DISPATCH(BB, CC, FF)                                                   \
-  if (bf16 == BB && causal == CC && out_f32 == FF)                                \
-    return d256::launch_variant<256, BB, CC, FF>(q, k, v, p, static_cast<int>(grid), stream);
-  TA_DISPATCH(false, false, false) TA_DISPATCH(false, false, true)
-  TA_DISPATCH(false, true, false) TA_DISPATCH(false, true, true)
-  TA_DISPATCH(true, false, false) TA_DISPATCH(true, false, true)
-  TA_DISPATCH(true, true, false) TA_DISPATCH(true, true, true)
+#define TA_DISPATCH(DD, BB, CC, FF)                                               \
+  if (D == DD && bf16 == BB && causal == CC && out_f32 == FF)                     \
+    return shared_kv::launch_variant<DD, BB, CC, FF>(q, k, v, p, static_cast<int>(grid), stream);
+#define TA_DISPATCH4(DD)                                                          \
+  TA_DISPATCH(DD, false, false, false) TA_DISPATCH(DD, false, false, true)        \
+  TA_DISPATCH(DD, false, true, false) TA_DISPATCH(DD, false, true, true)          \
+  TA_DISPATCH(DD, true, false, false) TA_DISPATCH(DD, true, false, true)          \
+  TA_DISPATCH(DD, true, true, false) TA_DISPATCH(DD, true, true, true)
+  TA_DISPATCH4(128)
+  TA_DISPATCH4(256)
+#undef TA_DISPATCH4
 #undef TA_DISPATCH
   return cudaErrorInvalidValue;
 }
 
-int rows_per_cta_d256() { return d256::Layout<256>::kRowsPerCta; }
+int rows_per_cta_shared_kv(int D) {
+  return D == 256 ? shared_kv::Layout<256>::kRowsPerCta : shared_kv::Layout<128>::kRowsPerCta;
+}
 
 }  // namespace ta
