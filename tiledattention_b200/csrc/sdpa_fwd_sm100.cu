@@ -612,8 +612,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             p1 = ex2_approx(x1);
           }
           pk[i] = pack2<BF16>(p0, p1);
-          // The row sum uses the rounded weights the P.V MMA sees, so the output is an
-          // exact convex combination of V rows with those weights.
+          // Row sum of the rounded weights the P.V MMA sees, so the output is an exact
+          // convex combination of V rows with those weights (summing the fp32 weights is
+          // 3-10 % faster but differs by up to 2^-9 relative, which the sigma=4 parity
+          // cases expose when one weight dominates a row).
           add_packed16_to_f32<BF16>(pk[i], acc_lo[i % kSumChains], acc_hi[i % kSumChains]);
         }
         // P of this half's 64 keys: 32 columns of 16-bit pairs over the first half of this
