@@ -124,3 +124,48 @@ def test_padded_head_dims(D):
 def test_head_dim_256(S, causal, dtype):
     q, k, v = _inputs(1, 3, S, 256, dtype, S + 256)
     _check(q, k, v, causal)
+
+
+def test_long_rows_shared_kv_kernel():
+    """S >= 16384 at head dim 128 runs on the shared-K/V (two query tiles per CTA) kernel."""
+    q, k, v = _inputs(1, 1, 16384, 128, torch.bfloat16, 31)
+    _check(q, k, v, True, oracle_rows=(16384 - 96, 16384))
+    _check(q, k, v, False, oracle_rows=(0, 64))
+
+
+def test_scheduler_slots_reused_across_launches_and_streams():
+    """The persistent kernel takes a scheduler slot per launch from a fixed pool of 1024 and
+    the last CTA of a launch resets it: more launches than slots, alternating between two
+    streams, must give the same results as a single launch."""
+    import tiledattention_b200 as ta
+
+    dev = torch.device("cuda:0")
+    inputs = [[t.to(dev) for t in _inputs(1, 3, 700, 64, torch.float16, 40 + i)] for i in range(2)]
+    ref = [ta.sdpa(*inputs[i], causal=True) for i in range(2)]
+    torch.cuda.synchronize()
+    streams = [torch.cuda.Stream(dev), torch.cuda.Stream(dev)]
+    outs = [None, None]
+    for n in range(1100):
+        i = n % 2
+        with torch.cuda.stream(streams[i]):
+            outs[i] = ta.sdpa(*inputs[i], causal=True)
+    torch.cuda.synchronize()
+    ta.check_device_status(dev)
+    for i in range(2):
+        assert torch.equal(outs[i], ref[i])
+
+
+def test_torch_ops_match_python_api():
+    """torch.ops.tiledattention_b200.sdpa_fwd / sdpa_fwd_partial give the same results as the
+    Python API on the same inputs."""
+    import tiledattention_b200 as ta
+    import tiledattention_b200.ops  # noqa: F401
+
+    dev = torch.device("cuda:0")
+    q, k, v = (t.to(dev) for t in _inputs(2, 3, 333, 128, torch.bfloat16, 50))
+    o = torch.ops.tiledattention_b200.sdpa_fwd(q, k, v, True, 0.09)
+    assert torch.equal(o, ta.sdpa(q, k, v, causal=True, scale=0.09))
+    o_p, lse = torch.ops.tiledattention_b200.sdpa_fwd_partial(q, k, v, False, 0.09, 0, 333, 2)
+    o_r, lse_r = ta.sdpa_partial(q, k, v, causal=False, scale=0.09, n_split=2)
+    assert torch.equal(o_p, o_r) and torch.equal(lse, lse_r)
+    ta.check_device_status(dev)
