@@ -194,7 +194,7 @@ int run_forward(const void* q, const void* k, const void* v, void* o, bool out_f
   if ((rc = make_map(&mv, v, B, H, S, D, v_strides, dtype, "v"))) return rc;
   CUtensorMap mo;
   memset(&mo, 0, sizeof(mo));
-  if (!out_f32 && !ta::uses_shared_kv(D, S) &&
+  if (!out_f32 && !ta::uses_shared_kv(D, S, causal != 0) &&
       (rc = make_map(&mo, o, B, H, S, D, o_strides, dtype, "o")))
     return rc;
 
@@ -216,7 +216,8 @@ int run_forward(const void* q, const void* k, const void* v, void* o, bool out_f
   const int span = kv_end - kv_begin;
   p.split_len = ((span + n_split - 1) / n_split + 127) / 128 * 128;
   if (p.split_len == 0) p.split_len = 128;
-  p.n_qblk = (S + ta::rows_per_cta(D, S) - 1) / ta::rows_per_cta(D, S);
+  const int rows_per_item = ta::rows_per_cta(D, S, causal != 0);
+  p.n_qblk = (S + rows_per_item - 1) / rows_per_item;
   p.scale_log2 = static_cast<float>(static_cast<double>(scale) * 1.4426950408889634);
 #ifdef TA_TRACE
   p.trace = g_trace;

@@ -23,15 +23,26 @@ struct FwdParams {
   unsigned int* sched;     // {next work item, CTAs finished} of this launch (set by the launcher)
 };
 
-// Whether (D, S) runs on the shared-K/V kernel (sdpa_fwd_sm100_shared_kv.cu): head dim 256,
-// and head dim 128 from kSharedKvMinSeq keys on, where the persistent one-tile kernel's
-// lower start-up cost no longer outweighs loading each K/V tile once per 128 rows instead
-// of once per 256 (measured crossover between S = 4096 and 16384 on B200).
-constexpr int kSharedKvMinSeq = 16384;
-inline bool uses_shared_kv(int D, int S) { return D == 256 || (D == 128 && S >= kSharedKvMinSeq); }
+// Whether (D, S, causal) runs on the shared-K/V kernel (sdpa_fwd_sm100_shared_kv.cu): head
+// dim 256 always; head dim 128 from kSharedKvMinSeq keys on (causal) or
+// kSharedKvMinSeqNonCausal (non-causal), where the persistent one-tile kernel's lower
+// start-up cost no longer outweighs loading each K/V tile once per 128 query rows instead of
+// once per 256 (crossovers measured on B200).
+#ifndef TA_SKV_MIN_SEQ
+#define TA_SKV_MIN_SEQ 32768
+#endif
+#ifndef TA_SKV_MIN_SEQ_NONCAUSAL
+#define TA_SKV_MIN_SEQ_NONCAUSAL 16384
+#endif
+constexpr int kSharedKvMinSeq = TA_SKV_MIN_SEQ;
+constexpr int kSharedKvMinSeqNonCausal = TA_SKV_MIN_SEQ_NONCAUSAL;
+inline bool uses_shared_kv(int D, int S, bool causal) {
+  return D == 256 ||
+         (D == 128 && S >= (causal ? kSharedKvMinSeq : kSharedKvMinSeqNonCausal));
+}
 
-// Query rows one CTA (one work item of the persistent kernel) covers for (D, S).
-int rows_per_cta(int D, int S);
+// Query rows one CTA (one work item of the persistent kernel) covers for (D, S, causal).
+int rows_per_cta(int D, int S, bool causal);
 
 // The shared-K/V kernel, reached through launch_sdpa_fwd.
 cudaError_t launch_sdpa_fwd_shared_kv(const CUtensorMap& q, const CUtensorMap& k,
