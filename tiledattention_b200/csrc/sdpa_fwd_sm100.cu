@@ -24,8 +24,8 @@
 // when its max grows by more than 2^8, which is exact after the final division by l.
 //
 // Work: one item = one (key slice, batch*head pair, 128-row query block). The grid has at
-// most one CTA per SM; each CTA takes items from a global counter (bh-major order, the
-// longest causal blocks of a pair first) until they run out. Consecutive items of a CTA
+// most one CTA per SM; each CTA takes items from a global counter until they run out, in
+// groups of (b,h) pairs whose K/V fit in L2, longest causal blocks of a group first. Consecutive items of a CTA
 // overlap: while the softmax warps write the output of item i, the producer has loaded
 // Q and the first K tiles of item i+1 and the QK^T issuer has computed its first scores.
 //
@@ -210,14 +210,20 @@ struct Item {
   int split, bh, b, h, q_row0, kv_lo, kv_hi, n_kv;
 };
 
+// Item order: key slice, then groups of group_bh (b,h) pairs whose K/V fit in L2 together;
+// inside a group the longest causal query blocks of all its pairs come first (so the
+// dynamic scheduler ends each group, and the launch, on short items), pairs interleaved.
 template <bool CAUSAL>
 __device__ __forceinline__ Item decode_item(const FwdParams& p, int item) {
   Item it;
   const int per_split = p.BH * p.n_qblk;
   it.split = item / per_split;
   const int rem = item - it.split * per_split;
-  it.bh = rem / p.n_qblk;
-  const int qblk = p.n_qblk - 1 - (rem % p.n_qblk);  // longest causal rows of a pair first
+  const int group = rem / (p.group_bh * p.n_qblk);
+  const int within = rem - group * (p.group_bh * p.n_qblk);
+  const int gsize = min(p.group_bh, p.BH - group * p.group_bh);
+  const int qblk = p.n_qblk - 1 - within / gsize;
+  it.bh = group * p.group_bh + within % gsize;
   it.b = it.bh / p.H;
   it.h = it.bh % p.H;
   it.q_row0 = qblk * kRowsPerTile;
@@ -853,6 +859,14 @@ cudaError_t launch_sdpa_fwd(const CUtensorMap& q, const CUtensorMap& k, const CU
     g_sm_count[dev].store(sms, std::memory_order_release);
   }
   FwdParams p = p_in;
+  // (b,h) pairs per scheduling group: as many as have K and V (S x D x 16-bit each) within
+  // 48 MB, a good part of the 126 MB L2, so their re-reads stay on chip.
+#ifndef TA_SCHED_GROUP_MB
+#define TA_SCHED_GROUP_MB 48
+#endif
+  const long long kv_bytes = 4ll * p.S * D;
+  const long long group = (static_cast<long long>(TA_SCHED_GROUP_MB) << 20) / (kv_bytes > 0 ? kv_bytes : 1);
+  p.group_bh = static_cast<int>(group < 1 ? 1 : (group > p.BH ? p.BH : group));
   const unsigned int slot = g_sched_next[dev].fetch_add(1, std::memory_order_relaxed) % kSchedSlots;
   p.sched = g_sched_base[dev].load(std::memory_order_relaxed) + 2 * slot;
   const int grid = static_cast<int>(items < sms ? items : sms);

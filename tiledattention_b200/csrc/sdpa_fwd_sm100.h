@@ -21,6 +21,7 @@ struct FwdParams {
   unsigned long long timeout_ns;  // limit of every in-kernel wait (0: 1 s)
   int selftest_stall;      // 1: the MMA warp waits on a barrier nothing arrives on
   unsigned int* sched;     // {next work item, CTAs finished} of this launch (set by the launcher)
+  int group_bh;            // persistent kernel: (b,h) pairs per scheduling group (see decode)
 };
 
 // Whether (D, S, causal) runs on the shared-K/V kernel (sdpa_fwd_sm100_shared_kv.cu): head
