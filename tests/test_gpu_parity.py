@@ -171,3 +171,27 @@ def test_torch_ops_match_python_api():
     o_r, lse_r = ta.sdpa_partial(q, k, v, causal=False, scale=0.09, n_split=2)
     assert torch.equal(o_p, o_r) and torch.equal(lse, lse_r)
     ta.check_device_status(dev)
+
+
+def test_cuda_graph_capture_and_replay():
+    """A captured forward replays correctly: the persistent kernel's scheduler slot is fixed
+    at capture time and reset by the kernel itself after every run."""
+    import tiledattention_b200 as ta
+
+    dev = torch.device("cuda:0")
+    q, k, v = (t.to(dev) for t in _inputs(2, 4, 1500, 128, torch.bfloat16, 60))
+    ref = ta.sdpa(q, k, v, causal=True)  # also performs the one-time initialisation
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        ta.sdpa(q, k, v, causal=True)  # warm-up on the capture stream
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph, stream=stream):
+            out = ta.sdpa(q, k, v, causal=True)
+    for _ in range(3):
+        out.zero_()
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref)
+    ta.check_device_status(dev)
