@@ -198,6 +198,15 @@ const char* ta_last_error(void);
  */
 void ta_debug_set_selftest(int stall, unsigned long long timeout_ns);
 
+/*
+ * ta_debug_set_cta_pair — process-wide switch (off by default) that runs head-dim-128 work
+ * below the shared-K/V crossover on the CTA-pair kernel: 2-CTA clusters issuing
+ * tcgen05 cta_group::2 MMAs over 256-row items, each CTA loading half of every K/V tile.
+ * Same results (parity-tested); measured ~7 % slower than the default single-CTA kernel on
+ * B200, kept for experiments. No reference counterpart.
+ */
+void ta_debug_set_cta_pair(int on);
+
 /* ta_abi_version — ABI version of this library (major*100 + minor). */
 int ta_abi_version(void);
 

@@ -195,3 +195,23 @@ def test_cuda_graph_capture_and_replay():
         torch.cuda.synchronize()
         assert torch.equal(out, ref)
     ta.check_device_status(dev)
+
+
+@pytest.mark.parametrize("case", [(2, 3, 1000, True, torch.bfloat16), (1, 2, 3001, False, torch.float16),
+                                  (1, 4, 4096, True, torch.bfloat16), (1, 1, 129, True, torch.float16)])
+def test_cta_pair_kernel_parity(case):
+    """The experimental CTA-pair kernel (2-CTA clusters, cta_group::2 MMAs), switched on at
+    run time, gives the same-tolerance results as the default kernel."""
+    from tiledattention_b200 import _native
+
+    B, H, S, causal, dtype = case
+    lib = _native.load_library()
+    lib.ta_debug_set_cta_pair(1)
+    try:
+        q, k, v = _inputs(B, H, S, 128, dtype, 70 + S)
+        if S >= 4096:
+            _check(q, k, v, causal, oracle_rows=(S - 128, S))
+        else:
+            _check(q, k, v, causal)
+    finally:
+        lib.ta_debug_set_cta_pair(0)

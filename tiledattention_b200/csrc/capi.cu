@@ -55,7 +55,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 // 4-D map over a [B,H,S,D] operand: dims (D, S, H, B), box 64 x 128 x 1 x 1,
 // 128-byte swizzle, zero fill out of bounds (ragged sequence tail).
 int make_map(CUtensorMap* map, const void* base, int B, int H, int S, int D,
-             const int64_t* st, int dtype, const char* name) {
+             const int64_t* st, int dtype, const char* name, unsigned box_rows = 128) {
   auto enc = encode_fn();
   if (!enc) return fail(TA_ERR_DRIVER, "cuTensorMapEncodeTiled entry point unavailable");
   const uint64_t esz = 2;
@@ -80,7 +80,7 @@ int make_map(CUtensorMap* map, const void* base, int B, int H, int S, int D,
     gstride[i] = s;
     span = s * static_cast<uint64_t>(ext[i]);
   }
-  cuuint32_t box[4] = {64, 128, 1, 1};
+  cuuint32_t box[4] = {64, box_rows, 1, 1};
   cuuint32_t estride[4] = {1, 1, 1, 1};
   CUresult r = enc(map, dtype == TA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
@@ -107,12 +107,18 @@ int check_device() {
 #ifdef TA_TRACE
 unsigned long long* g_trace = nullptr;
 #endif
+// Experimental CTA-pair kernel switch (ta_debug_set_cta_pair); off by default.
+std::atomic<int> g_cta_pair{0};
 // Failure-path self-test settings (ta_debug_set_selftest); off by default.
 std::atomic<int> g_selftest_stall{0};
 std::atomic<unsigned long long> g_timeout_ns{0};
 }  // namespace
 
 int ta_capi_fail(int code, const char* msg) { return fail(code, "%s", msg); }
+
+namespace ta {
+bool cta_pair_requested() { return g_cta_pair.load(std::memory_order_relaxed) != 0; }
+}  // namespace ta
 void ta_capi_clear_error() { g_last_error.clear(); }
 
 extern "C" {
@@ -129,6 +135,8 @@ void ta_debug_set_selftest(int stall, unsigned long long timeout_ns) {
   g_selftest_stall.store(stall ? 1 : 0);
   g_timeout_ns.store(timeout_ns);
 }
+
+void ta_debug_set_cta_pair(int on) { g_cta_pair.store(on ? 1 : 0); }
 
 const char* ta_last_error(void) { return g_last_error.c_str(); }
 
@@ -197,6 +205,11 @@ int run_forward(const void* q, const void* k, const void* v, void* o, bool out_f
   if (!out_f32 && !ta::uses_shared_kv(D, S, causal != 0) &&
       (rc = make_map(&mo, o, B, H, S, D, o_strides, dtype, "o")))
     return rc;
+  CUtensorMap mk64;
+  memset(&mk64, 0, sizeof(mk64));
+  if (ta::uses_pair(D, S, causal != 0) &&
+      (rc = make_map(&mk64, k, B, H, S, D, k_strides, dtype, "k", 64)))
+    return rc;
 
   ta::FwdParams p{};
   p.o = o;
@@ -224,7 +237,7 @@ int run_forward(const void* q, const void* k, const void* v, void* o, bool out_f
 #endif
   p.timeout_ns = g_timeout_ns.load();
   p.selftest_stall = g_selftest_stall.load();
-  cudaError_t err = ta::launch_sdpa_fwd(mq, mk, mv, mo, p, D, dtype == TA_DTYPE_BF16,
+  cudaError_t err = ta::launch_sdpa_fwd(mq, mk, mv, mo, mk64, p, D, dtype == TA_DTYPE_BF16,
                                         causal != 0, out_f32, static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess)
     return fail(TA_ERR_CUDA, "kernel launch failed: %s", cudaGetErrorString(err));
