@@ -23,8 +23,6 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#include <stdio.h>
-
 #include <atomic>
 
 #include "sm100_pair.cuh"
@@ -803,12 +801,6 @@ cudaError_t launch_variant(const CUtensorMap& q, const CUtensorMap& k64, const C
     err = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
     if (err != cudaSuccess) return err;
     max_pairs = clusters > 0 ? clusters : 1;
-#ifdef TA_PAIR_FORCE_CLUSTERS
-    max_pairs = TA_PAIR_FORCE_CLUSTERS;
-#endif
-#ifdef TA_PAIR_REPORT
-    printf("pair kernel: %d co-resident clusters\n", clusters);
-#endif
     g_max_pairs[dev].store(max_pairs, std::memory_order_release);
   }
   const long long pairs = items < max_pairs ? items : max_pairs;

@@ -79,7 +79,6 @@ constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;      // log2 units
-#define MMA_WAIT mbar_wait_bounded
 constexpr int kSumChains = 4;  // independent row-sum accumulators (short dependency chains)
 #ifndef TA_POLY_EVERY
 #define TA_POLY_EVERY 0
@@ -323,7 +322,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool more = (j + 1 < n_kv);
         const int st_k = it % L::kStages;
         // query tile 0
-        ok = MMA_WAIT(&bars->p_full[0], j & 1, abort_flag, kTimeoutNs);
+        ok = mbar_wait_bounded(&bars->p_full[0], j & 1, abort_flag, kTimeoutNs);
         if (!ok) break;
         TRACE(j, 8);
         tc_fence_after();
@@ -341,7 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if constexpr (L::kTiles == 2) {
           // query tile 1
           TRACE(j, 9);
-          ok = MMA_WAIT(&bars->p_full[1], j & 1, abort_flag, kTimeoutNs);
+          ok = mbar_wait_bounded(&bars->p_full[1], j & 1, abort_flag, kTimeoutNs);
           if (!ok) break;
           TRACE(j, 10);
           tc_fence_after();

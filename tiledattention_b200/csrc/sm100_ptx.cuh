@@ -49,22 +49,11 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
-#ifndef TA_WAIT_HINT_NS
-#define TA_WAIT_HINT_NS 0
-#endif
-// try_wait may suspend the thread in hardware until the phase completes or a time hint
-// elapses, which keeps waiting warps from spending issue slots on polling.
+// try_wait may suspend the thread in hardware until the phase completes or a
+// system-dependent time limit elapses, which keeps waiting warps from spending issue slots
+// on polling.
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity) {
   uint32_t ok;
-#if TA_WAIT_HINT_NS > 0
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar_addr), "r"(parity), "n"(TA_WAIT_HINT_NS)
-      : "memory");
-#else
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
@@ -72,42 +61,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
       : "=r"(ok)
       : "r"(bar_addr), "r"(parity)
       : "memory");
-#endif
   return ok != 0;
 }
 
 // Wait until the phase with the given parity of `bar` has completed, or give up.
 // Gives up when `abort_flag` (shared) becomes non-zero or after `timeout_ns` of
 // global time; returns false in both cases. Never spins unbounded.
-__device__ __forceinline__ bool mbar_test_wait(uint32_t bar_addr, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar_addr), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Same contract as mbar_wait_bounded, polling with the non-suspending test_wait
-// (lowest wake-up latency; for the single MMA-issuing thread).
-__device__ __forceinline__ bool mbar_spin_bounded(uint64_t* bar, uint32_t parity,
-                                                  volatile int* abort_flag,
-                                                  uint64_t timeout_ns) {
-  const uint32_t a = smem_u32(bar);
-  if (mbar_test_wait(a, parity)) return true;
-  const uint64_t t0 = global_timer_ns();
-  for (uint32_t it = 1;; ++it) {
-    if (mbar_test_wait(a, parity)) return true;
-    if ((it & 255u) == 0u) {
-      if (*abort_flag) return false;
-      if (global_timer_ns() - t0 > timeout_ns) return false;
-    }
-  }
-}
-
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
                                                   volatile int* abort_flag,
                                                   uint64_t timeout_ns) {
@@ -338,11 +297,6 @@ __device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
-// Barrier over `count` threads (a multiple of 32) of the CTA on hardware barrier `id` (1-15).
-__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
-
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
