@@ -128,11 +128,11 @@ def test_head_dim_256(S, causal, dtype):
 
 def test_long_rows_shared_kv_kernel():
     """Long head-dim-128 rows run on the shared-K/V (two query tiles per CTA) kernel:
-    non-causal from S = 16384, causal from S = 32768."""
+    non-causal from S = 16384, causal from S = 65536."""
     q, k, v = _inputs(1, 1, 16384, 128, torch.bfloat16, 31)
     _check(q, k, v, False, oracle_rows=(0, 64))
-    q, k, v = _inputs(1, 1, 32768, 128, torch.bfloat16, 32)
-    _check(q, k, v, True, oracle_rows=(32768 - 64, 32768))
+    q, k, v = _inputs(1, 1, 65536, 128, torch.bfloat16, 32)
+    _check(q, k, v, True, oracle_rows=(65536 - 32, 65536))
 
 
 def test_scheduler_slots_reused_across_launches_and_streams():

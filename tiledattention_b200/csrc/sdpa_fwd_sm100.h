@@ -30,7 +30,7 @@ struct FwdParams {
 // start-up cost no longer outweighs loading each K/V tile once per 128 query rows instead of
 // once per 256 (crossovers measured on B200).
 #ifndef TA_SKV_MIN_SEQ
-#define TA_SKV_MIN_SEQ 32768
+#define TA_SKV_MIN_SEQ 65536
 #endif
 #ifndef TA_SKV_MIN_SEQ_NONCAUSAL
 #define TA_SKV_MIN_SEQ_NONCAUSAL 16384
