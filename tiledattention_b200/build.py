@@ -21,7 +21,7 @@ CSRC = os.path.join(PKG_DIR, "csrc")
 OUT_DIR = os.path.join(PKG_DIR, "_lib")
 OUT = os.path.join(OUT_DIR, "libtiledattention_b200.so")
 SOURCES = ["capi.cu", "sdpa_fwd_sm100.cu", "sdpa_fwd_sm100_shared_kv.cu", "sdpa_fwd_sm100_pair.cu", "lse_combine.cu", "noalloc_split.cu", "peer_merge.cu"]
-HEADERS = ["sm100_ptx.cuh", "sm100_pair.cuh", "sdpa_fwd_sm100.h", "lse_combine.h", "capi_internal.h"]
+HEADERS = ["sm100_ptx.cuh", "sm100_pair.cuh", "sdpa_common.cuh", "sdpa_fwd_sm100.h", "lse_combine.h", "capi_internal.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

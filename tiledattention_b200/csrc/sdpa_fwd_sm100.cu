@@ -60,11 +60,17 @@
 
 #include <atomic>
 
+#include "sdpa_common.cuh"
 #include "sm100_ptx.cuh"
 #include "sdpa_fwd_sm100.h"
 #include "tiledattention_b200.h"
 
 namespace ta {
+
+using common::add_packed16_to_f32;
+using common::Item;
+using common::pack2;
+using common::report;
 
 constexpr int kRowsPerTile = 128;  // query rows per item (= TMEM lanes)
 constexpr int kKeysPerTile = 128;  // keys per K/V tile
@@ -151,11 +157,6 @@ struct Barriers {
 };
 static_assert(sizeof(Barriers) <= 512, "barrier block");
 
-__device__ __forceinline__ void report(const FwdParams& p, uint32_t code, volatile int* abort_flag) {
-  *abort_flag = 1;
-  if (p.status) atomicOr(p.status, code);
-}
-
 #ifdef TA_TRACE
 // Experiment builds only: clock64 of event `ev` (< 16) of tile j (< 32) of the first
 // item of the first 64 blocks, for timeline analysis.
@@ -180,60 +181,6 @@ __device__ __forceinline__ void trace_item(const FwdParams& p, int ic, int ev) {
 #define TRACE(ic, j, ev)
 #define TRACE_ITEM(ic, ev)
 #endif
-
-// Two fp32 values -> one 32-bit word of two 16-bit values, `lo` in the low half.
-template <bool BF16>
-__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
-  uint32_t r;
-  if constexpr (BF16)
-    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
-  else
-    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
-  return r;
-}
-
-// acc_lo += low 16-bit value of w, acc_hi += high one (fp32 accumulation of bf16/fp16).
-template <bool BF16>
-__device__ __forceinline__ void add_packed16_to_f32(uint32_t w, float& acc_lo, float& acc_hi) {
-  if constexpr (BF16)
-    asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
-        "add.rn.f32.bf16 %0, lo, %0;\n\tadd.rn.f32.bf16 %1, hi, %1;\n\t}"
-        : "+f"(acc_lo), "+f"(acc_hi) : "r"(w));
-  else
-    asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
-        "add.rn.f32.f16 %0, lo, %0;\n\tadd.rn.f32.f16 %1, hi, %1;\n\t}"
-        : "+f"(acc_lo), "+f"(acc_hi) : "r"(w));
-}
-
-// One work item decoded: key slice, (b, h) pair, query block and its key-tile count.
-struct Item {
-  int split, bh, b, h, q_row0, kv_lo, kv_hi, n_kv;
-};
-
-// Item order: key slice, then groups of group_bh (b,h) pairs whose K/V fit in L2 together;
-// inside a group the longest causal query blocks of all its pairs come first (so the
-// dynamic scheduler ends each group, and the launch, on short items), pairs interleaved.
-template <bool CAUSAL>
-__device__ __forceinline__ Item decode_item(const FwdParams& p, int item) {
-  Item it;
-  const int per_split = p.BH * p.n_qblk;
-  it.split = item / per_split;
-  const int rem = item - it.split * per_split;
-  const int group = rem / (p.group_bh * p.n_qblk);
-  const int within = rem - group * (p.group_bh * p.n_qblk);
-  const int gsize = min(p.group_bh, p.BH - group * p.group_bh);
-  const int qblk = p.n_qblk - 1 - within / gsize;
-  it.bh = group * p.group_bh + within % gsize;
-  it.b = it.bh / p.H;
-  it.h = it.bh % p.H;
-  it.q_row0 = qblk * kRowsPerTile;
-  // keys [kv_lo, kv_hi) take part (the whole range, or one slice for split-KV)
-  it.kv_lo = min(p.kv_end, p.kv_begin + it.split * p.split_len);
-  it.kv_hi = min(p.kv_end, it.kv_lo + p.split_len);
-  const int kv_rows = CAUSAL ? min(it.kv_hi, it.q_row0 + kRowsPerTile) : it.kv_hi;
-  it.n_kv = kv_rows > it.kv_lo ? (kv_rows - it.kv_lo + kKeysPerTile - 1) / kKeysPerTile : 0;
-  return it;
-}
 
 // OUT_F32: write o as fp32 (the normalised partial output of one key slice) instead of
 // the input dtype. Items: n_split x B*H x n_qblk; slice s covers keys
@@ -364,7 +311,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int item = static_cast<int>(atomicAdd(&p.sched[0], 1u));
         TRACE_ITEM(ic, 5);
         Item w;
-        if (item < n_items) w = decode_item<CAUSAL>(p, item);
+        if (item < n_items) w = common::decode_item<CAUSAL, kRowsPerTile, kKeysPerTile>(p, item);
         else w.split = kNoItem;
         int* pub = bars->item[slot];
         pub[0] = w.split; pub[1] = w.bh; pub[2] = w.b; pub[3] = w.h;

@@ -25,6 +25,7 @@
 
 #include <atomic>
 
+#include "sdpa_common.cuh"
 #include "sm100_pair.cuh"
 #include "sm100_ptx.cuh"
 #include "sdpa_fwd_sm100.h"
@@ -32,6 +33,11 @@
 
 namespace ta {
 namespace pair {
+
+using common::add_packed16_to_f32;
+using common::Item;
+using common::pack2;
+using common::report;
 
 constexpr int kRowsPerTile = 128;  // query rows per CTA (= TMEM lanes)
 constexpr int kRowsPerItem = 256;  // query rows per CTA pair
@@ -105,11 +111,6 @@ struct Barriers {
 };
 static_assert(sizeof(Barriers) <= 512, "barrier block");
 
-__device__ __forceinline__ void report(const FwdParams& p, uint32_t code, volatile int* abort_flag) {
-  *abort_flag = 1;
-  if (p.status) atomicOr(p.status, code);
-}
-
 #ifdef TA_TRACE
 __device__ __forceinline__ void trace_ev(const FwdParams& p, int item_no, int j, int ev) {
   if (p.trace && item_no == 0 && blockIdx.x < 64 && j < 24) {
@@ -122,56 +123,6 @@ __device__ __forceinline__ void trace_ev(const FwdParams& p, int item_no, int j,
 #else
 #define TRACE(ic, j, ev)
 #endif
-
-template <bool BF16>
-__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
-  uint32_t r;
-  if constexpr (BF16)
-    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
-  else
-    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
-  return r;
-}
-
-template <bool BF16>
-__device__ __forceinline__ void add_packed16_to_f32(uint32_t w, float& acc_lo, float& acc_hi) {
-  if constexpr (BF16)
-    asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
-        "add.rn.f32.bf16 %0, lo, %0;\n\tadd.rn.f32.bf16 %1, hi, %1;\n\t}"
-        : "+f"(acc_lo), "+f"(acc_hi) : "r"(w));
-  else
-    asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
-        "add.rn.f32.f16 %0, lo, %0;\n\tadd.rn.f32.f16 %1, hi, %1;\n\t}"
-        : "+f"(acc_lo), "+f"(acc_hi) : "r"(w));
-}
-
-// One work item as seen by one CTA: q_row0 is this CTA's first query row; n_kv is the
-// pair's key-tile count (both CTAs run the same MMAs).
-struct Item {
-  int split, bh, b, h, q_row0, kv_lo, kv_hi, n_kv;
-};
-
-// Item order as in the single-CTA kernel, over 256-row query blocks.
-template <bool CAUSAL>
-__device__ __forceinline__ Item decode_item(const FwdParams& p, int item) {
-  Item it;
-  const int per_split = p.BH * p.n_qblk;
-  it.split = item / per_split;
-  const int rem = item - it.split * per_split;
-  const int group = rem / (p.group_bh * p.n_qblk);
-  const int within = rem - group * (p.group_bh * p.n_qblk);
-  const int gsize = min(p.group_bh, p.BH - group * p.group_bh);
-  const int qblk = p.n_qblk - 1 - within / gsize;
-  it.bh = group * p.group_bh + within % gsize;
-  it.b = it.bh / p.H;
-  it.h = it.bh % p.H;
-  it.q_row0 = qblk * kRowsPerItem;
-  it.kv_lo = min(p.kv_end, p.kv_begin + it.split * p.split_len);
-  it.kv_hi = min(p.kv_end, it.kv_lo + p.split_len);
-  const int kv_rows = CAUSAL ? min(it.kv_hi, it.q_row0 + kRowsPerItem) : it.kv_hi;
-  it.n_kv = kv_rows > it.kv_lo ? (kv_rows - it.kv_lo + kKeysPerTile - 1) / kKeysPerTile : 0;
-  return it;
-}
 
 template <int D, bool BF16, bool CAUSAL, bool OUT_F32>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -324,7 +275,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           const int item = static_cast<int>(atomicAdd(&p.sched[0], 1u));
-          if (item < n_items) w = decode_item<CAUSAL>(p, item);
+          if (item < n_items) w = common::decode_item<CAUSAL, kRowsPerItem, kKeysPerTile>(p, item);
           else w.split = kNoItem;
           int* pub = bars->item[slot];
           const int vals[8] = {w.split, w.bh, w.b, w.h, w.q_row0, w.kv_lo, w.kv_hi, w.n_kv};

@@ -46,12 +46,17 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "sdpa_common.cuh"
 #include "sm100_ptx.cuh"
 #include "sdpa_fwd_sm100.h"
 #include "tiledattention_b200.h"
 
 namespace ta {
 namespace shared_kv {
+
+using common::add_packed16_to_f32;
+using common::pack2;
+using common::report;
 
 constexpr int kRowsPerTile = 128;  // query rows per tile (= TMEM lanes)
 // Query tiles per CTA: two 128-row tiles up to D=128; one at D=256, where S (128) + O (256)
@@ -114,11 +119,6 @@ struct Barriers {
 };
 static_assert(sizeof(Barriers) <= 256, "barrier block");
 
-__device__ __forceinline__ void report(const FwdParams& p, uint32_t code, volatile int* abort_flag) {
-  *abort_flag = 1;
-  if (p.status) atomicOr(p.status, code);
-}
-
 #ifdef TA_TRACE
 // Experiment builds only: clock64 of event `ev` (< 16) of key tile j (< 32) in the
 // first 64 blocks, for timeline analysis.
@@ -133,30 +133,6 @@ __device__ __forceinline__ void trace_ev(const FwdParams& p, int j, int ev) {
 #else
 #define TRACE(j, ev)
 #endif
-
-// Two fp32 values -> one 32-bit word of two 16-bit values, `lo` in the low half.
-template <bool BF16>
-__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
-  uint32_t r;
-  if constexpr (BF16)
-    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
-  else
-    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
-  return r;
-}
-
-// acc_lo += low 16-bit value of w, acc_hi += high one (fp32 accumulation of bf16/fp16).
-template <bool BF16>
-__device__ __forceinline__ void add_packed16_to_f32(uint32_t w, float& acc_lo, float& acc_hi) {
-  if constexpr (BF16)
-    asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
-        "add.rn.f32.bf16 %0, lo, %0;\n\tadd.rn.f32.bf16 %1, hi, %1;\n\t}"
-        : "+f"(acc_lo), "+f"(acc_hi) : "r"(w));
-  else
-    asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
-        "add.rn.f32.f16 %0, lo, %0;\n\tadd.rn.f32.f16 %1, hi, %1;\n\t}"
-        : "+f"(acc_lo), "+f"(acc_hi) : "r"(w));
-}
 
 // OUT_F32: write o as fp32 (the normalised partial output of one key slice) instead of
 // the input dtype. Grid = n_split x B*H x n_qblk; slice s covers keys
