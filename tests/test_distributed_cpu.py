@@ -142,3 +142,18 @@ def test_rank_that_never_joins_is_detected():
     res = dict(out_q.get(timeout=10) for _ in range(2))
     assert res[1] == "left"
     assert res[0].startswith("error")
+
+
+def test_row_share_partitions_rows():
+    """The peer-memory merge's per-rank query-row shares tile [0, S) exactly, in rank order,
+    with sizes differing by at most one."""
+    from tiledattention_b200.distributed import row_share
+
+    for seq_len in (1, 7, 128, 1000, 65536):
+        for world in (1, 2, 3, 4, 8):
+            shares = [row_share(seq_len, world, r) for r in range(world)]
+            assert shares[0][0] == 0 and shares[-1][1] == seq_len
+            for (a0, a1), (b0, b1) in zip(shares, shares[1:]):
+                assert a1 == b0
+            sizes = [b - a for a, b in shares]
+            assert max(sizes) - min(sizes) <= 1
