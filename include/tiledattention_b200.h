@@ -38,7 +38,7 @@ extern "C" {
 /* Status codes. */
 #define TA_OK                   0
 #define TA_ERR_INVALID_ARGUMENT 1  /* null pointer, non-positive size, bad scale      */
-#define TA_ERR_UNSUPPORTED_DIM  2  /* head dim not in {64, 128, 256}                  */
+#define TA_ERR_UNSUPPORTED_DIM  2  /* head dim not runnable as given (see ta_sdpa_fwd)  */
 #define TA_ERR_UNSUPPORTED_DTYPE 3 /* dtype not TA_DTYPE_F16 / TA_DTYPE_BF16          */
 #define TA_ERR_LAYOUT           4  /* stride / alignment not expressible as a TMA map */
 #define TA_ERR_CUDA             5  /* a CUDA runtime call failed (see ta_last_error)  */
@@ -72,6 +72,9 @@ extern "C" {
  *
  *   q, k, v       device pointers, dtype `dtype`, [B,H,S,D] with the given strides
  *   o             device pointer for the output, same dtype, [B,H,S,D] with o_strides
+ *   D             head dim: 64, 128 or 256; or a multiple of 8 below 128, which runs on the
+ *                 next native kernel without padded copies where that kernel allows
+ *                 (otherwise TA_ERR_UNSUPPORTED_DIM: zero-pad to 64 / 128 / 256 and retry)
  *   lse           optional device float32 [B*H*S] (row-major over (b,h,s)); receives the
  *                 natural-log log-sum-exp of the scaled, masked scores per query row.
  *                 Pass NULL to skip (the reference has no lse output).

@@ -112,10 +112,29 @@ def test_strided_bshd_layout():
     _check(q, k, v, True)
 
 
-@pytest.mark.parametrize("D", [32, 80, 96, 160, 192])
-def test_padded_head_dims(D):
+@pytest.mark.parametrize("D", [8, 32, 48, 72, 80, 96, 120, 100, 160, 192])
+@pytest.mark.parametrize("causal", [False, True])
+def test_other_head_dims(D, causal):
+    """Multiples of 8 below 128 run without padding (zero-filled loads, clipped stores);
+    D=100 and D > 128 are zero-padded by the launcher."""
     q, k, v = _inputs(1, 2, 200, D, torch.float16, D)
-    _check(q, k, v, False)
+    _check(q, k, v, causal)
+
+
+def test_unpadded_head_dim_strided_and_lse():
+    """Head dim 96 from [B,S,H,D] storage (no copy) with the log-sum-exp output."""
+    import tiledattention_b200 as ta
+
+    g = torch.Generator().manual_seed(96)
+    base = [torch.randn(2, 333, 4, 96, generator=g).to(torch.bfloat16) for _ in range(3)]
+    q, k, v = (t.transpose(1, 2) for t in base)
+    _check(q, k, v, True)
+    dev = torch.device("cuda:0")
+    o, lse = ta.sdpa_with_lse(q.to(dev), k.to(dev), v.to(dev), causal=True)
+    s = (q.float() @ k.float().mT) / math.sqrt(96)
+    mask = torch.ones(333, 333, dtype=torch.bool).tril()
+    ref_lse = torch.logsumexp(s.masked_fill(~mask, float("-inf")), dim=-1)
+    assert float((lse.cpu() - ref_lse).abs().max()) < 4e-3
 
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])

@@ -176,8 +176,21 @@ int run_forward(const void* q, const void* k, const void* v, void* o, bool out_f
     return fail(TA_ERR_INVALID_ARGUMENT, "null pointer argument");
   if (B <= 0 || H <= 0 || S <= 0)
     return fail(TA_ERR_INVALID_ARGUMENT, "B, H, S must be positive (got %d, %d, %d)", B, H, S);
-  if (D != 64 && D != 128 && D != 256)
-    return fail(TA_ERR_UNSUPPORTED_DIM, "head dim %d not in {64, 128, 256}", D);
+  // Kernel head dim: 64, 128 and 256 are native. A head dim below 128 that is a multiple of
+  // 8 runs on the next native kernel with tensor maps over its true extent: loads zero-fill
+  // the missing columns (which add nothing to q.k and give zero output columns) and the
+  // output TMA store clips them, so no padded copies are needed. That needs the kernels with
+  // a TMA-stored 16-bit output (not the shared-K/V kernel, not fp32 partials); elsewhere the
+  // caller pads (TA_ERR_UNSUPPORTED_DIM).
+  int kd = D;
+  if (D != 64 && D != 128 && D != 256) {
+    if (D < 8 || D > 128 || D % 8 != 0)
+      return fail(TA_ERR_UNSUPPORTED_DIM,
+                  "head dim %d: native 64, 128, 256, or a multiple of 8 below 128", D);
+    kd = D <= 64 ? 64 : 128;
+    if (out_f32 || ta::uses_shared_kv(kd, S, causal != 0))
+      return fail(TA_ERR_UNSUPPORTED_DIM, "head dim %d needs padding to %d on this path", D, kd);
+  }
   if (dtype != TA_DTYPE_F16 && dtype != TA_DTYPE_BF16)
     return fail(TA_ERR_UNSUPPORTED_DTYPE, "dtype code %d", dtype);
   if (!(scale > 0.f) || !std::isfinite(scale))
@@ -202,12 +215,12 @@ int run_forward(const void* q, const void* k, const void* v, void* o, bool out_f
   if ((rc = make_map(&mv, v, B, H, S, D, v_strides, dtype, "v"))) return rc;
   CUtensorMap mo;
   memset(&mo, 0, sizeof(mo));
-  if (!out_f32 && !ta::uses_shared_kv(D, S, causal != 0) &&
+  if (!out_f32 && !ta::uses_shared_kv(kd, S, causal != 0) &&
       (rc = make_map(&mo, o, B, H, S, D, o_strides, dtype, "o")))
     return rc;
   CUtensorMap mk64;
   memset(&mk64, 0, sizeof(mk64));
-  if (ta::uses_pair(D, S, causal != 0) &&
+  if (ta::uses_pair(kd, S, causal != 0) &&
       (rc = make_map(&mk64, k, B, H, S, D, k_strides, dtype, "k", 64)))
     return rc;
 
@@ -229,7 +242,7 @@ int run_forward(const void* q, const void* k, const void* v, void* o, bool out_f
   const int span = kv_end - kv_begin;
   p.split_len = ((span + n_split - 1) / n_split + 127) / 128 * 128;
   if (p.split_len == 0) p.split_len = 128;
-  const int rows_per_item = ta::rows_per_cta(D, S, causal != 0);
+  const int rows_per_item = ta::rows_per_cta(kd, S, causal != 0);
   p.n_qblk = (S + rows_per_item - 1) / rows_per_item;
   p.scale_log2 = static_cast<float>(static_cast<double>(scale) * 1.4426950408889634);
 #ifdef TA_TRACE
@@ -237,7 +250,7 @@ int run_forward(const void* q, const void* k, const void* v, void* o, bool out_f
 #endif
   p.timeout_ns = g_timeout_ns.load();
   p.selftest_stall = g_selftest_stall.load();
-  cudaError_t err = ta::launch_sdpa_fwd(mq, mk, mv, mo, mk64, p, D, dtype == TA_DTYPE_BF16,
+  cudaError_t err = ta::launch_sdpa_fwd(mq, mk, mv, mo, mk64, p, kd, dtype == TA_DTYPE_BF16,
                                         causal != 0, out_f32, static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess)
     return fail(TA_ERR_CUDA, "kernel launch failed: %s", cudaGetErrorString(err));

@@ -95,6 +95,9 @@ def run_sdpa_fwd(q, k, v, *, causal: bool, scale: float, return_lse: bool = Fals
     """Launch the sm_100a kernel. Inputs are already validated ([B,H,S,D], fp16/bf16, CUDA).
 
     Returns o (and the float32 [B,H,S] natural-log log-sum-exp when return_lse=True).
+    Head dims 64/128/256 run natively; a multiple of 8 below 128 first runs without padded
+    copies (the kernel zero-fills the missing columns on load and clips them on store), and
+    only where that path is not available are q, k, v zero-padded to the next native size.
     """
     torch_mod = _runtime.get_torch_module()
     lib = _runtime.get_native_library()
@@ -107,20 +110,12 @@ def run_sdpa_fwd(q, k, v, *, causal: bool, scale: float, return_lse: bool = Fals
     else:  # validated earlier; kept for direct callers
         raise DTypeNotSupportedError("q dtype must be torch.float16 or torch.bfloat16.")
 
-    out = torch_mod.empty((batch, heads, seq_len, kdim), dtype=q.dtype, device=q.device)
     lse = None
     if return_lse:
         lse = torch_mod.empty((batch, heads, seq_len), dtype=torch_mod.float32, device=q.device)
-    if out.numel() == 0:
-        o = out[..., :head_dim] if kdim != head_dim else out
-        return (o, lse) if return_lse else o
-
-    if kdim != head_dim:
-        pad = (0, kdim - head_dim)
-        q = torch_mod.nn.functional.pad(q, pad)
-        k = torch_mod.nn.functional.pad(k, pad)
-        v = torch_mod.nn.functional.pad(v, pad)
-    q, k, v = (t if _tma_compatible(t) else t.contiguous() for t in (q, k, v))
+    if q.numel() == 0:
+        out = torch_mod.empty((batch, heads, seq_len, head_dim), dtype=q.dtype, device=q.device)
+        return (out, lse) if return_lse else out
 
     mode = _sync_mode()
     dev_idx = q.device.index if q.device.index is not None else torch_mod.cuda.current_device()
@@ -131,29 +126,38 @@ def run_sdpa_fwd(q, k, v, *, causal: bool, scale: float, return_lse: bool = Fals
         stream = _raw_stream(torch_mod, dev_idx)
         if mode == "strict":
             torch_mod.cuda.synchronize(q.device)
-        st = _native.strides16(q.stride(), k.stride(), v.stride(), out.stride())
-        rc = lib.ta_sdpa_fwd(
-            q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
-            lse.data_ptr() if lse is not None else None,
-            batch, heads, seq_len, kdim, st[0], st[1], st[2], st[3],
-            dtype_code, 1 if causal else 0, float(scale), status.data_ptr(), stream,
-        )
-        if rc == _native.TA_ERR_LAYOUT and not all(t.is_contiguous() for t in (q, k, v)):
-            q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
-            st = _native.strides16(q.stride(), k.stride(), v.stride(), out.stride())
-            rc = lib.ta_sdpa_fwd(
-                q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+
+        def launch(qq, kk, vv, out, dim):
+            st = _native.strides16(qq.stride(), kk.stride(), vv.stride(), out.stride())
+            return lib.ta_sdpa_fwd(
+                qq.data_ptr(), kk.data_ptr(), vv.data_ptr(), out.data_ptr(),
                 lse.data_ptr() if lse is not None else None,
-                batch, heads, seq_len, kdim, st[0], st[1], st[2], st[3],
+                batch, heads, seq_len, dim, st[0], st[1], st[2], st[3],
                 dtype_code, 1 if causal else 0, float(scale), status.data_ptr(), stream,
             )
+
+        rc = _native.TA_ERR_UNSUPPORTED_DIM
+        if kdim == head_dim or (head_dim % 8 == 0 and head_dim < 128):
+            out = torch_mod.empty((batch, heads, seq_len, head_dim), dtype=q.dtype,
+                                  device=q.device)
+            qa, ka, va = (t if _tma_compatible(t) else t.contiguous() for t in (q, k, v))
+            rc = launch(qa, ka, va, out, head_dim)
+            if rc == _native.TA_ERR_LAYOUT and not all(t.is_contiguous() for t in (qa, ka, va)):
+                qa, ka, va = qa.contiguous(), ka.contiguous(), va.contiguous()
+                rc = launch(qa, ka, va, out, head_dim)
+        if rc == _native.TA_ERR_UNSUPPORTED_DIM and kdim != head_dim:
+            # Zero-pad to the next native head dim (flash_fwd.py:868-872 pads the same way).
+            pad = (0, kdim - head_dim)
+            qp, kp, vp = (torch_mod.nn.functional.pad(t, pad) for t in (q, k, v))
+            full = torch_mod.empty((batch, heads, seq_len, kdim), dtype=q.dtype, device=q.device)
+            rc = launch(qp, kp, vp, full, kdim)
+            out = full[..., :head_dim]
         if rc != _native.TA_OK:
             _raise_for(lib, rc)
         if mode in ("post", "strict"):
             check_device_status(q.device)
 
-    o = out[..., :head_dim] if kdim != head_dim else out
-    return (o, lse) if return_lse else o
+    return (out, lse) if return_lse else out
 
 
 def _dtype_code(torch_mod, dtype):
