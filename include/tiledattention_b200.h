@@ -72,9 +72,9 @@ extern "C" {
  *
  *   q, k, v       device pointers, dtype `dtype`, [B,H,S,D] with the given strides
  *   o             device pointer for the output, same dtype, [B,H,S,D] with o_strides
- *   D             head dim: 64, 128 or 256; or a multiple of 8 below 128, which runs on the
- *                 next native kernel without padded copies where that kernel allows
- *                 (otherwise TA_ERR_UNSUPPORTED_DIM: zero-pad to 64 / 128 / 256 and retry)
+ *   D             head dim: 64, 128 or 256 natively; any other multiple of 8 up to 256 runs
+ *                 on the next native kernel without padded copies; other head dims give
+ *                 TA_ERR_UNSUPPORTED_DIM (zero-pad to 64 / 128 / 256 and retry)
  *   lse           optional device float32 [B*H*S] (row-major over (b,h,s)); receives the
  *                 natural-log log-sum-exp of the scaled, masked scores per query row.
  *                 Pass NULL to skip (the reference has no lse output).

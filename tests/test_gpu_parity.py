@@ -112,11 +112,12 @@ def test_strided_bshd_layout():
     _check(q, k, v, True)
 
 
-@pytest.mark.parametrize("D", [8, 32, 48, 72, 80, 96, 120, 100, 160, 192])
+@pytest.mark.parametrize("D", [8, 32, 48, 72, 80, 96, 120, 136, 160, 192, 248, 100, 200])
 @pytest.mark.parametrize("causal", [False, True])
 def test_other_head_dims(D, causal):
-    """Multiples of 8 below 128 run without padding (zero-filled loads, clipped stores);
-    D=100 and D > 128 are zero-padded by the launcher."""
+    """Multiples of 8 run without padding (zero-filled loads, output written for the true
+    columns only: clipped TMA store on the persistent kernel, predicated stores on the
+    shared-K/V kernel for D > 128); D=100 is zero-padded by the launcher."""
     q, k, v = _inputs(1, 2, 200, D, torch.float16, D)
     _check(q, k, v, causal)
 
@@ -250,3 +251,10 @@ def test_head_dim_64_long_rows_fp16():
     rows in fp16, checked on the last rows."""
     q, k, v = _inputs(1, 4, 8192, 64, torch.float16, 81)
     _check(q, k, v, True, oracle_rows=(8192 - 96, 8192))
+
+
+def test_unpadded_head_dim_on_shared_kv_kernel():
+    """Head dim 96 over a non-causal S=16384 runs on the shared-K/V kernel at kernel head dim
+    128 with predicated output stores (no padded copies)."""
+    q, k, v = _inputs(1, 1, 16384, 96, torch.bfloat16, 97)
+    _check(q, k, v, False, oracle_rows=(0, 64))

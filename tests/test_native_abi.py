@@ -57,9 +57,10 @@ def _call(lib, D=128, dtype=1, scale=0.1, null_q=False, S=64, ostride3=1):
 
 def test_argument_validation_without_gpu(lib):
     assert _call(lib, null_q=True) == _native.TA_ERR_INVALID_ARGUMENT
-    # native 64/128/256, or a multiple of 8 below 128 (run without padding); others rejected
+    # native 64/128/256, or another multiple of 8 up to 256 (run without padding); others
+    # rejected
     assert _call(lib, D=100) == _native.TA_ERR_UNSUPPORTED_DIM
-    assert _call(lib, D=160) == _native.TA_ERR_UNSUPPORTED_DIM
+    assert _call(lib, D=264) == _native.TA_ERR_UNSUPPORTED_DIM
     assert _call(lib, D=4) == _native.TA_ERR_UNSUPPORTED_DIM
     assert _call(lib, dtype=7) == _native.TA_ERR_UNSUPPORTED_DTYPE
     assert _call(lib, scale=0.0) == _native.TA_ERR_INVALID_ARGUMENT

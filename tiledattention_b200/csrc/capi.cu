@@ -176,20 +176,18 @@ int run_forward(const void* q, const void* k, const void* v, void* o, bool out_f
     return fail(TA_ERR_INVALID_ARGUMENT, "null pointer argument");
   if (B <= 0 || H <= 0 || S <= 0)
     return fail(TA_ERR_INVALID_ARGUMENT, "B, H, S must be positive (got %d, %d, %d)", B, H, S);
-  // Kernel head dim: 64, 128 and 256 are native. A head dim below 128 that is a multiple of
-  // 8 runs on the next native kernel with tensor maps over its true extent: loads zero-fill
-  // the missing columns (which add nothing to q.k and give zero output columns) and the
-  // output TMA store clips them, so no padded copies are needed. That needs the kernels with
-  // a TMA-stored 16-bit output (not the shared-K/V kernel, not fp32 partials); elsewhere the
-  // caller pads (TA_ERR_UNSUPPORTED_DIM).
+  // Kernel head dim: 64, 128 and 256 are native. Any other head dim that is a multiple of 8
+  // (up to 256) runs on the next native kernel with tensor maps over its true extent: loads
+  // zero-fill the missing columns (which add nothing to q.k and give zero output columns)
+  // and the output is written for the true columns only (clipped TMA store, or predicated
+  // 16-byte stores), so no padded copies are needed. Others: TA_ERR_UNSUPPORTED_DIM (the
+  // caller pads).
   int kd = D;
   if (D != 64 && D != 128 && D != 256) {
-    if (D < 8 || D > 128 || D % 8 != 0)
+    if (D < 8 || D > 256 || D % 8 != 0)
       return fail(TA_ERR_UNSUPPORTED_DIM,
-                  "head dim %d: native 64, 128, 256, or a multiple of 8 below 128", D);
-    kd = D <= 64 ? 64 : 128;
-    if (out_f32 || ta::uses_shared_kv(kd, S, causal != 0))
-      return fail(TA_ERR_UNSUPPORTED_DIM, "head dim %d needs padding to %d on this path", D, kd);
+                  "head dim %d: 64, 128, 256, or another multiple of 8 up to 256", D);
+    kd = D <= 64 ? 64 : (D <= 128 ? 128 : 256);
   }
   if (dtype != TA_DTYPE_F16 && dtype != TA_DTYPE_BF16)
     return fail(TA_ERR_UNSUPPORTED_DTYPE, "dtype code %d", dtype);
@@ -232,6 +230,7 @@ int run_forward(const void* q, const void* k, const void* v, void* o, bool out_f
   p.o_sh = o_strides[1];
   p.o_ss = o_strides[2];
   p.o_split_stride = o_split_stride;
+  p.d_out = D;
   p.S = S;
   p.H = H;
   p.BH = B * H;

@@ -677,7 +677,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                      static_cast<int64_t>(row) * p.o_ss + col0 + c * 32));
 #pragma unroll
             for (int i = 0; i < 8; ++i)
-              dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+              if (col0 + c * 32 + 4 * i < p.d_out)  // columns beyond the true head dim
+                dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
           }
         } else {
           // 32 output columns = four 16-byte units of the 128-byte-swizzled staging row

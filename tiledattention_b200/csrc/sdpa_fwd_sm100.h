@@ -22,6 +22,8 @@ struct FwdParams {
   int selftest_stall;      // 1: the MMA warp waits on a barrier nothing arrives on
   unsigned int* sched;     // {next work item, CTAs finished} of this launch (set by the launcher)
   int group_bh;            // persistent kernel: (b,h) pairs per scheduling group (see decode)
+  int d_out;               // head dim of the output (<= the kernel's; multiple of 8); the
+                           // kernel writes only these columns
 };
 
 // Whether (D, S, causal) runs on the shared-K/V kernel (sdpa_fwd_sm100_shared_kv.cu): head

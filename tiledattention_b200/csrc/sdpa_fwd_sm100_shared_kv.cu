@@ -520,8 +520,9 @@ __global__ void __launch_bounds__(kThreads, 1)
               float4* dst = reinterpret_cast<float4*>(orow + c * 128);
 #pragma unroll
               for (int i = 0; i < 8; ++i)
-                dst[i] = make_float4(__uint_as_float(o[4 * i]) * inv_l, __uint_as_float(o[4 * i + 1]) * inv_l,
-                                     __uint_as_float(o[4 * i + 2]) * inv_l, __uint_as_float(o[4 * i + 3]) * inv_l);
+                if (c * 32 + 4 * i < p.d_out)  // output columns beyond the true head dim
+                  dst[i] = make_float4(__uint_as_float(o[4 * i]) * inv_l, __uint_as_float(o[4 * i + 1]) * inv_l,
+                                       __uint_as_float(o[4 * i + 2]) * inv_l, __uint_as_float(o[4 * i + 3]) * inv_l);
             }
           } else {
             uint32_t pw[16];
@@ -533,7 +534,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               uint4* dst = reinterpret_cast<uint4*>(orow + c * 64);
 #pragma unroll
               for (int i = 0; i < 4; ++i)
-                dst[i] = make_uint4(pw[4 * i], pw[4 * i + 1], pw[4 * i + 2], pw[4 * i + 3]);
+                if (c * 32 + 8 * i < p.d_out)  // output columns beyond the true head dim
+                  dst[i] = make_uint4(pw[4 * i], pw[4 * i + 1], pw[4 * i + 2], pw[4 * i + 3]);
             }
           }
         }

@@ -95,9 +95,9 @@ def run_sdpa_fwd(q, k, v, *, causal: bool, scale: float, return_lse: bool = Fals
     """Launch the sm_100a kernel. Inputs are already validated ([B,H,S,D], fp16/bf16, CUDA).
 
     Returns o (and the float32 [B,H,S] natural-log log-sum-exp when return_lse=True).
-    Head dims 64/128/256 run natively; a multiple of 8 below 128 first runs without padded
-    copies (the kernel zero-fills the missing columns on load and clips them on store), and
-    only where that path is not available are q, k, v zero-padded to the next native size.
+    Head dims 64/128/256 run natively; another multiple of 8 runs without padded copies
+    (the kernel zero-fills the missing columns on load and writes only the true columns);
+    other head dims are zero-padded to the next native size.
     """
     torch_mod = _runtime.get_torch_module()
     lib = _runtime.get_native_library()
@@ -137,7 +137,7 @@ def run_sdpa_fwd(q, k, v, *, causal: bool, scale: float, return_lse: bool = Fals
             )
 
         rc = _native.TA_ERR_UNSUPPORTED_DIM
-        if kdim == head_dim or (head_dim % 8 == 0 and head_dim < 128):
+        if kdim == head_dim or head_dim % 8 == 0:
             out = torch_mod.empty((batch, heads, seq_len, head_dim), dtype=q.dtype,
                                   device=q.device)
             qa, ka, va = (t if _tma_compatible(t) else t.contiguous() for t in (q, k, v))
