@@ -163,3 +163,42 @@ def strides16(*stride_tuples):
 def describe_devstat(word: int) -> str:
     parts = [text for bit, text in DEVSTAT_BITS.items() if word & bit]
     return "; ".join(parts) if parts else f"status 0x{word:x}"
+
+
+_fast = None
+_fast_tried = False
+
+
+def load_fast_launch(lib):
+    """Load (once) the one-call host launcher (_lib/_fast_launch*.so, built from
+    csrc/fast_launch.cpp) and bind it to `lib`'s ta_sdpa_fwd. Returns the module, or None
+    when it is not built (the Python launch path then takes every call)."""
+    global _fast, _fast_tried
+    if not isinstance(lib, ctypes.CDLL):
+        return None
+    with _lock:
+        if _fast_tried:
+            return _fast
+        _fast_tried = True
+        if os.environ.get("TILEDATTN_FAST_LAUNCH", "1") == "0":
+            return None
+        import glob
+        import importlib.util
+
+        found = sorted(glob.glob(os.path.join(os.path.dirname(LIB_PATH), "_fast_launch*.so")))
+        if not found:
+            return None
+        spec = importlib.util.spec_from_file_location("tiledattention_b200._fast_launch", found[0])
+        mod = importlib.util.module_from_spec(spec)
+        try:
+            spec.loader.exec_module(mod)
+        except ImportError:  # built against another torch: the Python launch path remains
+            return None
+        mod.set_entry(ctypes.cast(lib.ta_sdpa_fwd, ctypes.c_void_p).value)
+        _fast = mod
+        return mod
+
+
+def fast_launch_module():
+    """The loaded one-call launcher module, or None."""
+    return _fast

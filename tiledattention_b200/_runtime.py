@@ -84,7 +84,15 @@ def require_supported_runtime() -> None:
                 f"Unsupported GPU: compute capability {major}.{minor}; "
                 "this build targets sm_100a (B200, compute capability 10.0)."
             )
-        _get_native_library()
+        lib = _get_native_library()
+        from . import _native
+
+        fast = _native.load_fast_launch(lib)
+        if fast is not None:  # status words created before the launcher was loaded
+            from .launch import _status_words
+
+            for idx, word in _status_words.items():
+                fast.set_status(idx, word.data_ptr())
         _runtime_ready = True
 
 

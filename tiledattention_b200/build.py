@@ -23,6 +23,9 @@ OUT = os.path.join(OUT_DIR, "libtiledattention_b200.so")
 SOURCES = ["capi.cu", "sdpa_fwd_sm100.cu", "sdpa_fwd_sm100_shared_kv.cu", "sdpa_fwd_sm100_pair.cu", "lse_combine.cu", "noalloc_split.cu", "peer_merge.cu"]
 HEADERS = ["sm100_ptx.cuh", "sm100_pair.cuh", "sdpa_common.cuh", "sdpa_fwd_sm100.h", "lse_combine.h", "capi_internal.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+# One-call host launcher (CPython extension over libtorch; no device code): see
+# csrc/fast_launch.cpp.
+FAST_SOURCE = "fast_launch.cpp"
 
 
 def nvcc_path() -> str:
@@ -41,7 +44,44 @@ def _stale() -> bool:
     return any(os.path.getmtime(d) > t for d in deps)
 
 
+def fast_launch_path() -> str:
+    import sysconfig
+
+    return os.path.join(OUT_DIR, "_fast_launch" + sysconfig.get_config_var("EXT_SUFFIX"))
+
+
+def build_fast_launch(force: bool = False) -> str:
+    """Compile csrc/fast_launch.cpp with the host C++ compiler against the installed torch."""
+    import sysconfig
+
+    import torch
+
+    out = fast_launch_path()
+    src = os.path.join(CSRC, FAST_SOURCE)
+    if not force and os.path.exists(out) and os.path.getmtime(out) >= os.path.getmtime(src):
+        return out
+    torch_dir = os.path.dirname(torch.__file__)
+    cuda_home = os.environ.get("CUDA_HOME") or os.path.dirname(os.path.dirname(nvcc_path()))
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    os.makedirs(OUT_DIR, exist_ok=True)
+    cmd = [
+        os.environ.get("CXX", "g++"), "-O2", "-std=c++17", "-fPIC", "-shared",
+        f"-D_GLIBCXX_USE_CXX11_ABI={abi}",
+        "-I", os.path.join(torch_dir, "include"),
+        "-I", os.path.join(torch_dir, "include", "torch", "csrc", "api", "include"),
+        "-I", os.path.join(cuda_home, "include"),
+        "-I", sysconfig.get_paths()["include"],
+        src, "-o", out + ".tmp",
+        "-L", os.path.join(torch_dir, "lib"), "-lc10", "-lc10_cuda", "-ltorch_cpu",
+        "-ltorch_python", "-Wl,-rpath," + os.path.join(torch_dir, "lib"),
+    ]
+    subprocess.run(cmd, check=True)
+    os.replace(out + ".tmp", out)
+    return out
+
+
 def build(force: bool = False, verbose: bool = False) -> str:
+    build_fast_launch(force)
     if not force and not _stale():
         return OUT
     os.makedirs(OUT_DIR, exist_ok=True)

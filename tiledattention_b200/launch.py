@@ -59,6 +59,9 @@ def _status_word(torch_mod, device):
     if word is None:
         word = torch_mod.zeros(1, dtype=torch_mod.int32, device=device)
         _status_words[idx] = word
+        fast = _native.fast_launch_module()
+        if fast is not None:
+            fast.set_status(idx, word.data_ptr())
     return word
 
 

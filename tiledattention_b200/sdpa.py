@@ -9,9 +9,10 @@ contract, then scale = 1/sqrt(D) of the original head dim, then the launch.
 from __future__ import annotations
 
 import math
+import os
 from numbers import Real
 
-from . import _runtime
+from . import _native, _runtime
 from ._errors import InvalidShapeError
 from .checks import validate_sdpa_inputs
 from .launch import run_lse_combine, run_sdpa_fwd, run_sdpa_partial
@@ -29,6 +30,23 @@ def _prepare(q, k, v, causal, scale):
     return float(scale) if scale is not None else 1.0 / math.sqrt(head_dim)
 
 
+def _fast_launch(q, k, v, causal, scale, want_lse):
+    """The one-call native launcher for the common case, or None (the full path then runs
+    and raises the reference's error, copies or pads as needed). Taken only once the runtime
+    gate has passed and with the default asynchronous sync mode."""
+    fast = _native._fast
+    if fast is None or not _runtime._runtime_ready:
+        return None
+    mode = os.environ.get("TILEDATTN_SYNC_MODE")
+    if mode is not None and mode.strip().lower() != "async":
+        return None
+    if scale is None:
+        scale = -1.0  # the launcher's code for 1/sqrt(D)
+    elif scale.__class__ is not float or not scale > 0:
+        return None
+    return fast.launch(q, k, v, causal, scale, want_lse)
+
+
 def sdpa(q, k, v, *, causal: bool = False, scale: float | None = None):
     """Scaled dot-product attention forward: softmax(q k^T * scale + mask) v.
 
@@ -38,6 +56,9 @@ def sdpa(q, k, v, *, causal: bool = False, scale: float | None = None):
     Returns a new [B, H, S, D] tensor of q's dtype, computed asynchronously on the
     current torch stream.
     """
+    out = _fast_launch(q, k, v, causal, scale, False)
+    if out is not None:
+        return out
     resolved_scale = _prepare(q, k, v, causal, scale)
     return run_sdpa_fwd(q, k, v, causal=causal, scale=resolved_scale)
 
@@ -47,6 +68,9 @@ def sdpa_with_lse(q, k, v, *, causal: bool = False, scale: float | None = None):
 
     The reference has no lse output; it is the building block of the split-KV merge.
     """
+    out = _fast_launch(q, k, v, causal, scale, True)
+    if out is not None:
+        return out
     resolved_scale = _prepare(q, k, v, causal, scale)
     return run_sdpa_fwd(q, k, v, causal=causal, scale=resolved_scale, return_lse=True)
 
