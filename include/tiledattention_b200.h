@@ -117,7 +117,7 @@ int ta_sdpa_fwd_partial(const void* q, const void* k, const void* v, float* o_pa
  * ta_lse_combine — merge n_split partial results (layout of ta_sdpa_fwd_partial) into
  * o [B,H,S,D] (element strides o_strides, dtype TA_DTYPE_F16 / BF16 / F32) and optional
  * lse [B*H*S]:  lse = log sum_s exp(lse_s),  o = sum_s exp(lse_s - lse) o_s.
- * No counterpart in the reference (which has no split-KV mode). Allocates nothing.
+ * D: any multiple of 8 up to 256 (else TA_ERR_UNSUPPORTED_DIM). No counterpart in the reference (which has no split-KV mode). Allocates nothing.
  */
 int ta_lse_combine(const float* o_part, const float* lse_part, int n_split,
                    int B, int H, int S, int D, void* o, const int64_t* o_strides,
@@ -142,7 +142,7 @@ int ta_peer_barrier(unsigned int* const* flags, int n_peers, int rank, unsigned 
 /*
  * ta_lse_merge_peers — log-sum-exp merge of n_src <= 16 split-KV states read directly from
  * the peers' memory: o_src[i] fp32 [B*H][S][D] and lse_src[i] fp32 [B*H*S] (natural log,
- * -inf for a slice without keys; D 64, 128 or 256). Rows s in [s_begin, s_end) of every
+ * -inf for a slice without keys; D a multiple of 8 up to 256). Rows s in [s_begin, s_end) of every
  * (b,h) are merged and written to each of the n_dst <= TA_MAX_PEERS outputs o_dst[j] (dtype
  * TA_DTYPE_F16 / BF16 / F32, element strides o_strides with unit last stride, row s at
  * b*o_strides[0] + h*o_strides[1] + (s - row_base)*o_strides[2]) and, where lse_dst[j] is

@@ -206,3 +206,13 @@ def test_padded_head_dim_policy():
         64, 64, 64, 128, 128, 128, 256, 256, 256]
     with pytest.raises(InvalidShapeError):
         padded_head_dim(257)
+
+
+def test_state_head_dim_policy():
+    from tiledattention_b200.launch import state_head_dim
+
+    # split-KV state keeps multiples of 8 unpadded; other head dims take the padded size
+    assert [state_head_dim(d) for d in (8, 64, 96, 100, 128, 160, 200, 248, 256, 1)] == [
+        8, 64, 96, 128, 128, 160, 200, 248, 256, 64]
+    with pytest.raises(InvalidShapeError):
+        state_head_dim(257)

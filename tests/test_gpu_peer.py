@@ -31,14 +31,16 @@ def _states(S=1000, D=128, n=4, dtype=torch.bfloat16):
     return q, o_part.contiguous(), lse_part.contiguous()
 
 
+@pytest.mark.parametrize("D", [128, 96])
 @pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32])
-def test_merge_matches_combine_and_row_window(out_dtype):
+def test_merge_matches_combine_and_row_window(out_dtype, D):
     from tiledattention_b200 import _native
     from tiledattention_b200.launch import _status_word, run_lse_combine
 
     lib = _native.load_library()
-    q, o_part, lse_part = _states()
-    n, B, H, S, D = o_part.shape
+    q, o_part, lse_part = _states(D=D)
+    n, B, H, S, D_state = o_part.shape
+    assert D_state == D  # multiples of 8 keep their own head dim in the state
     ref_o, ref_lse = run_lse_combine(o_part, lse_part, out_dtype=out_dtype, return_lse=True)
     o_srcs, o_a = _addr_array([o_part[i].data_ptr() for i in range(n)])
     l_srcs, l_a = _addr_array([lse_part[i].data_ptr() for i in range(n)])

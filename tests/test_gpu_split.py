@@ -51,6 +51,28 @@ def test_split_kv_matches_full(S, n_split, causal, D, dtype):
     assert np.abs(lse.cpu().numpy() - ref_lse).max() < LSE_TOL[dtype]
 
 
+@pytest.mark.parametrize("D", [40, 96, 100, 200])
+@pytest.mark.parametrize("causal", [False, True])
+def test_split_kv_other_head_dims(D, causal):
+    """Head dims that are not 64/128/256: multiples of 8 keep their own head dim in the
+    split-KV state (no padded copies, merged by the run-time-D merge kernel); others are
+    padded to the next native size and sliced."""
+    import tiledattention_b200 as ta
+
+    dtype = torch.float16
+    q, k, v = _inputs(1, 3, 700, D, dtype, D)
+    dev = torch.device("cuda:0")
+    qd, kd, vd = q.to(dev), k.to(dev), v.to(dev)
+    o, lse = ta.sdpa_split_kv(qd, kd, vd, causal=causal, n_split=3, return_lse=True)
+    o_p, l_p = ta.sdpa_partial(qd, kd, vd, causal=causal, n_split=3)
+    ta.check_device_status(dev)
+    assert o.shape == q.shape and o_p.shape[-1] == D
+    ref, ref_lse = oracle.sdpa_numpy(q, k, v, causal=causal, scale=D ** -0.5, return_lse=True)
+    ok, err = _bound_ok(o.float().cpu(), torch.from_numpy(ref), dtype)
+    assert ok, err
+    assert np.abs(lse.cpu().numpy() - ref_lse).max() < LSE_TOL[dtype]
+
+
 @pytest.mark.parametrize("causal", [False, True])
 @pytest.mark.parametrize("kv", [(0, 128), (128, 700), (256, 257), (640, 1000)])
 def test_partial_state_matches_oracle(kv, causal):

@@ -73,3 +73,18 @@ def test_argument_validation_without_gpu(lib):
 def test_devstat_description():
     assert "softmax" in _native.describe_devstat(4)
     assert "MMA" in _native.describe_devstat(2)
+
+
+def test_merge_head_dims_without_gpu(lib):
+    # The split-KV merges take any multiple of 8 up to 256 (the state of an unpadded head
+    # dim); other head dims are rejected before any device work.
+    st = _native.strides4([2 * 64 * 100, 64 * 100, 100, 1])
+    for D in (100, 4, 264):
+        rc = lib.ta_lse_combine(0x1000, 0x1000, 2, 1, 2, 64, D, 0x1000, st, 1, None, None)
+        assert rc == _native.TA_ERR_UNSUPPORTED_DIM, D
+    ptrs = (ctypes.c_void_p * 1)(0x1000)
+    fptrs = (ctypes.POINTER(ctypes.c_float) * 1)()
+    for D in (100, 4, 264):
+        rc = lib.ta_lse_merge_peers(ptrs, ptrs, 1, 1, 2, 64, D, 0, 64, ptrs, fptrs, 1, st, 64, 0,
+                                    1, None, None)
+        assert rc == _native.TA_ERR_UNSUPPORTED_DIM, D

@@ -288,8 +288,8 @@ int ta_lse_combine(const float* o_part, const float* lse_part, int n_split, int 
     return fail(TA_ERR_INVALID_ARGUMENT, "null pointer argument");
   if (B <= 0 || H <= 0 || S <= 0 || n_split < 1)
     return fail(TA_ERR_INVALID_ARGUMENT, "B, H, S, n_split must be positive");
-  if (D != 64 && D != 128 && D != 256)
-    return fail(TA_ERR_UNSUPPORTED_DIM, "head dim %d not in {64, 128, 256}", D);
+  if (D < 8 || D > 256 || D % 8 != 0)
+    return fail(TA_ERR_UNSUPPORTED_DIM, "head dim %d is not a multiple of 8 up to 256", D);
   if (out_dtype != TA_DTYPE_F16 && out_dtype != TA_DTYPE_BF16 && out_dtype != TA_DTYPE_F32)
     return fail(TA_ERR_UNSUPPORTED_DTYPE, "output dtype code %d", out_dtype);
   const int64_t esz = out_dtype == TA_DTYPE_F32 ? 4 : 2;

@@ -8,7 +8,7 @@
 // rescaling the reference applies across key tiles (flash_fwd.py:426-436), applied
 // across slices instead.
 //
-// Layout: o_part fp32 [n_split][B][H][S][D] contiguous, lse_part fp32 [n_split][B*H*S];
+// Layout: o_part fp32 [n_split][B][H][S][D] contiguous (D a multiple of 8 up to 256), lse_part fp32 [n_split][B*H*S];
 // output o [B,H,S,D] with element strides (f16 / bf16 / f32), optional lse [B*H*S].
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -19,10 +19,14 @@
 
 namespace ta {
 
-template <int D, int OUT>  // OUT: 0 f16, 1 bf16, 2 f32
+// DT: the head dim, or 0 for a head dim known at run time only (p.D, a multiple of 8 up to
+// 256: four columns per thread, rows of D/4 threads packed into the 256-thread block).
+template <int DT, int OUT>  // OUT: 0 f16, 1 bf16, 2 f32
 __global__ void __launch_bounds__(256) lse_combine_kernel(CombineParams p) {
-  constexpr int kThreadsPerRow = D / 4;
-  constexpr int kRowsPerBlock = 256 / kThreadsPerRow;
+  const int D = DT > 0 ? DT : p.D;
+  const int kThreadsPerRow = D / 4;
+  const int kRowsPerBlock = 256 / kThreadsPerRow;
+  if (threadIdx.x >= kRowsPerBlock * kThreadsPerRow) return;
   const int64_t rows = static_cast<int64_t>(p.BH) * p.S;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kRowsPerBlock + threadIdx.x / kThreadsPerRow;
   const int d0 = (threadIdx.x % kThreadsPerRow) * 4;
@@ -75,10 +79,15 @@ cudaError_t launch_lse_combine(const CombineParams& p, int D, int out_kind, cuda
   const int rows_per_block = 256 / (D / 4);
   const int64_t grid = (rows + rows_per_block - 1) / rows_per_block;
   if (grid > 0x7fffffffll) return cudaErrorInvalidValue;
+  CombineParams q = p;
+  q.D = D;
 #define TA_COMB(DD, OO) \
-  if (D == DD && out_kind == OO) { lse_combine_kernel<DD, OO><<<static_cast<int>(grid), 256, 0, stream>>>(p); return cudaGetLastError(); }
+  if ((DD == 0 || D == DD) && out_kind == OO) { lse_combine_kernel<DD, OO><<<static_cast<int>(grid), 256, 0, stream>>>(q); return cudaGetLastError(); }
   TA_COMB(64, 0) TA_COMB(64, 1) TA_COMB(64, 2) TA_COMB(128, 0) TA_COMB(128, 1) TA_COMB(128, 2)
   TA_COMB(256, 0) TA_COMB(256, 1) TA_COMB(256, 2)
+  if (D >= 8 && D <= 256 && D % 8 == 0) {
+    TA_COMB(0, 0) TA_COMB(0, 1) TA_COMB(0, 2)
+  }
 #undef TA_COMB
   return cudaErrorInvalidValue;
 }

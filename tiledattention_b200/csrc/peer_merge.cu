@@ -40,6 +40,7 @@ struct PeerMergeParams {
   const unsigned int* status;
   int64_t o_sb, o_sh, o_ss;
   int n_src, n_dst, BH, H, S, s_begin, s_end, out_rows, row_base;
+  int D;  // head dim (set by launch_merge)
 };
 
 __device__ __forceinline__ uint64_t global_timer_ns() {
@@ -84,10 +85,14 @@ __global__ void peer_barrier_kernel(BarrierParams p) {
   }
 }
 
-template <int D, int OUT>  // OUT: 0 f16, 1 bf16, 2 f32
+// DT: the head dim, or 0 for a head dim known at run time only (p.D, a multiple of 8 up to
+// 256: four columns per thread, rows of D/4 threads packed into the 256-thread block).
+template <int DT, int OUT>  // OUT: 0 f16, 1 bf16, 2 f32
 __global__ void __launch_bounds__(256) lse_merge_peers_kernel(PeerMergeParams p) {
-  constexpr int kThreadsPerRow = D / 4;
-  constexpr int kRowsPerBlock = 256 / kThreadsPerRow;
+  const int D = DT > 0 ? DT : p.D;
+  const int kThreadsPerRow = D / 4;
+  const int kRowsPerBlock = 256 / kThreadsPerRow;
+  if (threadIdx.x >= kRowsPerBlock * kThreadsPerRow) return;
   const int slice = p.s_end - p.s_begin;
   const int64_t rows = static_cast<int64_t>(p.BH) * slice;
   const int64_t r = static_cast<int64_t>(blockIdx.x) * kRowsPerBlock + threadIdx.x / kThreadsPerRow;
@@ -163,13 +168,18 @@ cudaError_t launch_merge(const PeerMergeParams& p, int D, int out_kind, cudaStre
   const int rows_per_block = 256 / (D / 4);
   const int64_t grid = (rows + rows_per_block - 1) / rows_per_block;
   if (grid > 0x7fffffffll) return cudaErrorInvalidValue;
+PeerMergeParams q = p;
+  q.D = D;
 #define TA_MERGE(DD, OO)                                                                   \
-  if (D == DD && out_kind == OO) {                                                        \
-    lse_merge_peers_kernel<DD, OO><<<static_cast<int>(grid), 256, 0, stream>>>(p);        \
+  if ((DD == 0 || D == DD) && out_kind == OO) {                                           \
+    lse_merge_peers_kernel<DD, OO><<<static_cast<int>(grid), 256, 0, stream>>>(q);        \
     return cudaGetLastError();                                                            \
   }
   TA_MERGE(64, 0) TA_MERGE(64, 1) TA_MERGE(64, 2) TA_MERGE(128, 0) TA_MERGE(128, 1)
   TA_MERGE(128, 2) TA_MERGE(256, 0) TA_MERGE(256, 1) TA_MERGE(256, 2)
+  if (D >= 8 && D <= 256 && D % 8 == 0) {
+    TA_MERGE(0, 0) TA_MERGE(0, 1) TA_MERGE(0, 2)
+  }
 #undef TA_MERGE
   return cudaErrorInvalidValue;
 }
@@ -215,8 +225,8 @@ extern "C" int ta_lse_merge_peers(const void* const* o_src, const void* const* l
   if (B <= 0 || H <= 0 || S <= 0 || s_begin < 0 || s_end > S || s_begin > s_end ||
       row_base < 0 || row_base > s_begin || s_end - row_base > out_rows)
     return ta_capi_fail(TA_ERR_INVALID_ARGUMENT, "bad sizes or row range");
-  if (D != 64 && D != 128 && D != 256)
-    return ta_capi_fail(TA_ERR_UNSUPPORTED_DIM, "head dim not in {64, 128, 256}");
+  if (D < 8 || D > 256 || D % 8 != 0)
+    return ta_capi_fail(TA_ERR_UNSUPPORTED_DIM, "head dim must be a multiple of 8 up to 256");
   if (out_dtype != TA_DTYPE_F16 && out_dtype != TA_DTYPE_BF16 && out_dtype != TA_DTYPE_F32)
     return ta_capi_fail(TA_ERR_UNSUPPORTED_DTYPE, "output dtype must be f16, bf16 or f32");
   const int64_t esz = out_dtype == TA_DTYPE_F32 ? 4 : 2;

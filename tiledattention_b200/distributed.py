@@ -270,12 +270,12 @@ def sdpa_split_kv_distributed(q, k, v, *, causal: bool = False, scale: float | N
     import torch
     import torch.distributed as dist
 
-    from .launch import padded_head_dim, run_lse_combine
+    from .launch import run_lse_combine, state_head_dim
     from .sdpa import _prepare, sdpa_partial
 
     if exchange == "peer":
         resolved = _prepare(q, k, v, causal, scale)
-        ex = peer_exchange_for(q, padded_head_dim(int(q.shape[-1])), group)
+        ex = peer_exchange_for(q, state_head_dim(int(q.shape[-1])), group)
         return ex.forward(q, k, v, causal=causal, scale=resolved, gather=True)
     if exchange != "collective":
         raise ValueError("exchange must be 'collective' or 'peer'")

@@ -53,6 +53,15 @@ def padded_head_dim(head_dim: int) -> int:
     )
 
 
+def state_head_dim(head_dim: int) -> int:
+    """Head dim of the split-KV state (partials, merged outputs) for an input head dim: the
+    head dim itself when it is a multiple of 8 (the kernels read and write it without
+    padding), else the padded native size."""
+    if head_dim % 8 == 0 and 0 < head_dim <= NATIVE_HEAD_DIMS[-1]:
+        return head_dim
+    return padded_head_dim(head_dim)
+
+
 def _status_word(torch_mod, device):
     idx = device.index if device.index is not None else torch_mod.cuda.current_device()
     word = _status_words.get(idx)
@@ -188,15 +197,15 @@ def run_sdpa_partial(q, k, v, *, causal: bool, scale: float, kv_begin: int = 0,
 
     Returns (o_part, lse_part): fp32 [n_split, B, H, S, Dk] (each slice normalised by its
     own row sum) and fp32 [n_split, B, H, S] natural-log log-sum-exp (-inf where a slice
-    has no valid key for the row). Dk is the kernel head dim (64, 128 or 256); padded head
-    dims are sliced off by the caller. Inputs are already validated. ``out`` = (o_part,
+    has no valid key for the row). Dk = state_head_dim(D): D itself for multiples of 8,
+    else the padded native size, whose extra columns the caller slices off. Inputs are already validated. ``out`` = (o_part,
     lse_part): contiguous fp32 tensors of those shapes to write into (e.g. views of a
     buffer the peers have mapped) instead of new ones.
     """
     torch_mod = _runtime.get_torch_module()
     lib = _runtime.get_native_library()
     batch, heads, seq_len, head_dim = (int(x) for x in q.shape)
-    kdim = padded_head_dim(head_dim)
+    kdim = state_head_dim(head_dim)
     kv_end = seq_len if kv_end is None else int(kv_end)
     dtype_code = _dtype_code(torch_mod, q.dtype)
     if out is not None:
