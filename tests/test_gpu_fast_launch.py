@@ -121,5 +121,9 @@ def test_host_time_per_call_is_lower():
     fast_us = per_call(lambda: ta.sdpa(q, k, v, causal=True))
     slow_us = per_call(lambda: run_sdpa_fwd(q, k, v, causal=True,
                                             scale=_prepare(q, k, v, True, None)))
-    print(f"host us/call: one-call launcher {fast_us:.1f}, Python launch path {slow_us:.1f}")
+    import tiledattention_b200.ops  # noqa: F401
+
+    op_us = per_call(lambda: torch.ops.tiledattention_b200.sdpa_fwd(q, k, v, True, 0.125))
+    print(f"host us/call: one-call launcher {fast_us:.1f}, Python launch path {slow_us:.1f}, "
+          f"torch operator {op_us:.1f}")
     assert fast_us < slow_us

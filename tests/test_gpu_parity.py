@@ -193,6 +193,36 @@ def test_torch_ops_match_python_api():
     ta.check_device_status(dev)
 
 
+def test_torch_ops_other_head_dims_strides_and_errors():
+    """The C++ operators pad head dims that are not multiples of 8, copy strides a tensor map
+    cannot describe, raise through TORCH_CHECK, and trace under torch.compile."""
+    import tiledattention_b200 as ta
+    import tiledattention_b200.ops as ops
+
+    assert ops.NATIVE_OPS
+    dev = torch.device("cuda:0")
+    for D in (100, 96):
+        q, k, v = (t.to(dev) for t in _inputs(1, 2, 300, D, torch.float16, D))
+        o = torch.ops.tiledattention_b200.sdpa_fwd(q, k, v, True, 0.1)
+        assert o.shape == q.shape and o.is_contiguous()
+        assert torch.equal(o, ta.sdpa(q, k, v, causal=True, scale=0.1).contiguous())
+        o_p, lse = torch.ops.tiledattention_b200.sdpa_fwd_partial(q, k, v, True, 0.1, 0, 300, 2)
+        o_r, lse_r = ta.sdpa_partial(q, k, v, causal=True, scale=0.1, n_split=2)
+        assert o_p.shape[-1] == D and torch.equal(o_p, o_r) and torch.equal(lse, lse_r)
+    q, k, v = (t.to(dev) for t in _inputs(1, 2, 300, 64, torch.bfloat16, 3))
+    qs = torch.stack([q, q], dim=-1).flatten(-2)[..., ::2]  # head-dim stride 2
+    o = torch.ops.tiledattention_b200.sdpa_fwd(qs, k, v, False, 0.125)
+    assert torch.equal(o, ta.sdpa(q, k, v, scale=0.125))
+    with pytest.raises(RuntimeError, match="identical shapes"):
+        torch.ops.tiledattention_b200.sdpa_fwd(q, k[:, :1], v, False, 0.125)
+    with pytest.raises(RuntimeError, match="scale"):
+        torch.ops.tiledattention_b200.sdpa_fwd(q, k, v, False, -1.0)
+    f = torch.compile(lambda a, b, c: torch.ops.tiledattention_b200.sdpa_fwd(a, b, c, True, 0.125),
+                      backend="eager", fullgraph=True)
+    assert torch.equal(f(q, k, v), ta.sdpa(q, k, v, causal=True, scale=0.125))
+    ta.check_device_status(dev)
+
+
 def test_cuda_graph_capture_and_replay():
     """A captured forward replays correctly: the persistent kernel's scheduler slot is fixed
     at capture time and reset by the kernel itself after every run."""

@@ -171,8 +171,10 @@ _fast_tried = False
 
 def load_fast_launch(lib):
     """Load (once) the one-call host launcher (_lib/_fast_launch*.so, built from
-    csrc/fast_launch.cpp) and bind it to `lib`'s ta_sdpa_fwd. Returns the module, or None
-    when it is not built (the Python launch path then takes every call)."""
+    csrc/fast_launch.cpp) and bind it to `lib`'s entry points. Loading it also registers the
+    C++ torch operators torch.ops.tiledattention_b200.sdpa_fwd / sdpa_fwd_partial. Returns
+    the module, or None when it is not built or disabled (the Python launch path then takes
+    every call and tiledattention_b200.ops registers the operators in Python)."""
     global _fast, _fast_tried
     if not isinstance(lib, ctypes.CDLL):
         return None
@@ -194,7 +196,9 @@ def load_fast_launch(lib):
             spec.loader.exec_module(mod)
         except ImportError:  # built against another torch: the Python launch path remains
             return None
-        mod.set_entry(ctypes.cast(lib.ta_sdpa_fwd, ctypes.c_void_p).value)
+        addr = lambda fn: ctypes.cast(fn, ctypes.c_void_p).value  # noqa: E731
+        mod.set_entry(addr(lib.ta_sdpa_fwd))
+        mod.bind_ops(addr(lib.ta_sdpa_fwd_partial), addr(lib.ta_last_error))
         _fast = mod
         return mod
 

@@ -58,7 +58,9 @@ def build_fast_launch(force: bool = False) -> str:
 
     out = fast_launch_path()
     src = os.path.join(CSRC, FAST_SOURCE)
-    if not force and os.path.exists(out) and os.path.getmtime(out) >= os.path.getmtime(src):
+    deps = (src, os.path.join(REPO_DIR, "include", "tiledattention_b200.h"))
+    if not force and os.path.exists(out) and all(
+            os.path.getmtime(out) >= os.path.getmtime(d) for d in deps):
         return out
     torch_dir = os.path.dirname(torch.__file__)
     cuda_home = os.environ.get("CUDA_HOME") or os.path.dirname(os.path.dirname(nvcc_path()))
@@ -71,6 +73,7 @@ def build_fast_launch(force: bool = False) -> str:
         "-I", os.path.join(torch_dir, "include", "torch", "csrc", "api", "include"),
         "-I", os.path.join(cuda_home, "include"),
         "-I", sysconfig.get_paths()["include"],
+        "-I", os.path.join(REPO_DIR, "include"),
         src, "-o", out + ".tmp",
         "-L", os.path.join(torch_dir, "lib"), "-lc10", "-lc10_cuda", "-ltorch_cpu",
         "-ltorch_python", "-Wl,-rpath," + os.path.join(torch_dir, "lib"),
