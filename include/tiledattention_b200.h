@@ -168,8 +168,8 @@ int ta_lse_merge_peers(const void* const* o_src, const void* const* lse_src, int
  * device address and should happen before any stream capture on that device; all calls on
  * a device share the array, so calls that overlap on the GPU race — order them (one
  * stream). Nothing needs clearing between calls: each call rewrites every entry it reads.
- * Arguments as for ta_sdpa_fwd (o: dtype of q; lse optional). No counterpart in the
- * reference.
+ * Arguments as for ta_sdpa_fwd (o: dtype of q; lse optional; D any multiple of 8 up to 256,
+ * else TA_ERR_UNSUPPORTED_DIM). No counterpart in the reference.
  */
 int ta_sdpa_fwd_split_noalloc(const void* q, const void* k, const void* v, void* o, float* lse,
                               int B, int H, int S, int D,

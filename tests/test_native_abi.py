@@ -88,3 +88,11 @@ def test_merge_head_dims_without_gpu(lib):
         rc = lib.ta_lse_merge_peers(ptrs, ptrs, 1, 1, 2, 64, D, 0, 64, ptrs, fptrs, 1, st, 64, 0,
                                     1, None, None)
         assert rc == _native.TA_ERR_UNSUPPORTED_DIM, D
+
+
+def test_noalloc_head_dims_without_gpu(lib):
+    st = _native.strides4([2 * 64 * 100, 64 * 100, 100, 1])
+    for D in (100, 4, 264):
+        rc = lib.ta_sdpa_fwd_split_noalloc(16, 16, 16, 16, None, 1, 2, 64, D, st, st, st, st,
+                                           _native.TA_DTYPE_BF16, 1, 0.1, 2, None, None)
+        assert rc == _native.TA_ERR_UNSUPPORTED_DIM, D

@@ -35,6 +35,8 @@ def test_noalloc_split_matches_regular_entry_point_twice():
     cases = [
         (torch.bfloat16, 1, 4, 3001, 128, True, 4),   # ragged S, causal
         (torch.float16, 2, 2, 1000, 64, False, 3),     # non-causal, head dim 64
+        (torch.bfloat16, 1, 2, 700, 256, True, 2),     # head dim 256 (shared-K/V kernel)
+        (torch.float16, 1, 3, 500, 96, False, 2),      # head dim 96, no padded copies
     ]
     for call in range(2):
         for dtype, B, H, S, D, causal, n_split in cases:

@@ -67,9 +67,11 @@ extern "C" int ta_sdpa_fwd_split_noalloc(const void* q, const void* k, const voi
                                          int dtype, int causal, float scale, int n_split,
                                          unsigned int* dev_status, void* stream) {
   ta_capi_clear_error();
-  if (B <= 0 || H <= 0 || S <= 0 || n_split < 1 || (D != 64 && D != 128))
-    return ta_capi_fail(TA_ERR_INVALID_ARGUMENT,
-                        "B, H, S, n_split must be positive and D 64 or 128");
+  if (B <= 0 || H <= 0 || S <= 0 || n_split < 1)
+    return ta_capi_fail(TA_ERR_INVALID_ARGUMENT, "B, H, S, n_split must be positive");
+  // The slice partials keep the caller's head dim (the forward writes only its columns).
+  if (D < 8 || D > 256 || D % 8 != 0)
+    return ta_capi_fail(TA_ERR_UNSUPPORTED_DIM, "head dim must be a multiple of 8 up to 256");
   const unsigned long long rows =
       static_cast<unsigned long long>(n_split) * B * H * static_cast<unsigned long long>(S);
   const unsigned long long o_bytes = rows * static_cast<unsigned long long>(D) * 4ull;
