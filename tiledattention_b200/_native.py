@@ -184,13 +184,14 @@ def load_fast_launch(lib):
         _fast_tried = True
         if os.environ.get("TILEDATTN_FAST_LAUNCH", "1") == "0":
             return None
-        import glob
         import importlib.util
+        import sysconfig
 
-        found = sorted(glob.glob(os.path.join(os.path.dirname(LIB_PATH), "_fast_launch*.so")))
-        if not found:
+        path = os.path.join(os.path.dirname(LIB_PATH),
+                            "_fast_launch" + sysconfig.get_config_var("EXT_SUFFIX"))
+        if not os.path.exists(path):  # not built for this interpreter
             return None
-        spec = importlib.util.spec_from_file_location("tiledattention_b200._fast_launch", found[0])
+        spec = importlib.util.spec_from_file_location("tiledattention_b200._fast_launch", path)
         mod = importlib.util.module_from_spec(spec)
         try:
             spec.loader.exec_module(mod)
