@@ -191,6 +191,11 @@ def load_fast_launch(lib):
                             "_fast_launch" + sysconfig.get_config_var("EXT_SUFFIX"))
         if not os.path.exists(path):  # not built for this interpreter
             return None
+        import torch
+
+        stamp = path + ".torch"
+        if not os.path.exists(stamp) or open(stamp).read().strip() != torch.__version__:
+            return None  # built against another torch: its C++ ABI may differ
         spec = importlib.util.spec_from_file_location("tiledattention_b200._fast_launch", path)
         mod = importlib.util.module_from_spec(spec)
         try:

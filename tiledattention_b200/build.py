@@ -59,7 +59,9 @@ def build_fast_launch(force: bool = False) -> str:
     out = fast_launch_path()
     src = os.path.join(CSRC, FAST_SOURCE)
     deps = (src, os.path.join(REPO_DIR, "include", "tiledattention_b200.h"))
-    if not force and os.path.exists(out) and all(
+    stamp = out + ".torch"  # the torch version the module was built against (C++ ABI)
+    built_for = open(stamp).read().strip() if os.path.exists(stamp) else None
+    if not force and os.path.exists(out) and built_for == torch.__version__ and all(
             os.path.getmtime(out) >= os.path.getmtime(d) for d in deps):
         return out
     torch_dir = os.path.dirname(torch.__file__)
@@ -80,6 +82,8 @@ def build_fast_launch(force: bool = False) -> str:
     ]
     subprocess.run(cmd, check=True)
     os.replace(out + ".tmp", out)
+    with open(stamp, "w") as f:
+        f.write(torch.__version__ + "\n")
     return out
 
 
