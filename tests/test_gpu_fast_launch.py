@@ -127,3 +127,44 @@ def test_host_time_per_call_is_lower():
     print(f"host us/call: one-call launcher {fast_us:.1f}, Python launch path {slow_us:.1f}, "
           f"torch operator {op_us:.1f}")
     assert fast_us < slow_us
+
+
+def test_concurrent_host_threads_on_their_own_streams():
+    """The operator is re-entrant (the reference guards only its runtime initialisation with
+    a lock, _runtime.py:14,169): host threads launching at the same time, each on its own
+    stream, get the results of sequential calls."""
+    import threading
+
+    import tiledattention_b200 as ta
+
+    _fast()
+    shapes = [(1, 4, 700, 128, True), (2, 2, 513, 64, False), (1, 3, 300, 96, True),
+              (1, 2, 1025, 128, False)]
+    inputs = [_inputs(B, H, S, D, torch.bfloat16, 20 + i) for i, (B, H, S, D, _) in
+              enumerate(shapes)]
+    refs = [ta.sdpa(q, k, v, causal=c) for (q, k, v), (*_, c) in zip(inputs, shapes)]
+    torch.cuda.synchronize()
+    results = [[None] * 20 for _ in shapes]
+    errors = []
+
+    def worker(i):
+        try:
+            s = torch.cuda.Stream()
+            q, k, v = inputs[i]
+            with torch.cuda.stream(s):
+                for r in range(20):
+                    results[i][r] = ta.sdpa(q, k, v, causal=shapes[i][4])
+            s.synchronize()
+        except Exception as exc:  # reported below
+            errors.append(exc)
+
+    threads = [threading.Thread(target=worker, args=(i,)) for i in range(len(shapes))]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    assert not errors, errors
+    ta.check_device_status(DEV)
+    for i, ref in enumerate(refs):
+        for out in results[i]:
+            assert torch.equal(out, ref)
