@@ -262,6 +262,7 @@ int ta_sdpa_fwd(const void* q, const void* k, const void* v, void* o, float* lse
                 int S, int D, const int64_t* q_strides, const int64_t* k_strides,
                 const int64_t* v_strides, const int64_t* o_strides, int dtype, int causal,
                 float scale, unsigned int* dev_status, void* stream) {
+  TaNvtxRange nvtx_range("ta_sdpa_fwd");
   g_last_error.clear();
   return run_forward(q, k, v, o, false, o_strides, 0, lse, B, H, S, D, q_strides, k_strides,
                      v_strides, dtype, causal, scale, 0, S, 1, dev_status, stream);
@@ -272,6 +273,7 @@ int ta_sdpa_fwd_partial(const void* q, const void* k, const void* v, float* o_pa
                         const int64_t* k_strides, const int64_t* v_strides, int dtype,
                         int causal, float scale, int kv_begin, int kv_end, int n_split,
                         unsigned int* dev_status, void* stream) {
+  TaNvtxRange nvtx_range("ta_sdpa_fwd_partial");
   g_last_error.clear();
   if (!lse_part) return fail(TA_ERR_INVALID_ARGUMENT, "lse_part must not be null");
   const int64_t st[4] = {static_cast<int64_t>(H) * S * D, static_cast<int64_t>(S) * D, D, 1};
@@ -283,6 +285,7 @@ int ta_sdpa_fwd_partial(const void* q, const void* k, const void* v, float* o_pa
 int ta_lse_combine(const float* o_part, const float* lse_part, int n_split, int B, int H, int S,
                    int D, void* o, const int64_t* o_strides, int out_dtype, float* lse,
                    void* stream) {
+  TaNvtxRange nvtx_range("ta_lse_combine");
   g_last_error.clear();
   if (!o_part || !lse_part || !o || !o_strides)
     return fail(TA_ERR_INVALID_ARGUMENT, "null pointer argument");

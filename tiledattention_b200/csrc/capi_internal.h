@@ -3,6 +3,8 @@
 
 #include <stdint.h>
 
+#include <nvtx3/nvToolsExt.h>
+
 // Argument checks, tensor maps and the launch of the SDPA forward kernel; out_f32 selects
 // the fp32 (split-KV partial) output. Defined in capi.cu.
 int run_forward(const void* q, const void* k, const void* v, void* o, bool out_f32,
@@ -14,3 +16,12 @@ int run_forward(const void* q, const void* k, const void* v, void* o, bool out_f
 // Record an error message for ta_last_error() and return `code`.
 int ta_capi_fail(int code, const char* msg);
 void ta_capi_clear_error();
+
+// NVTX range named after the entry point, open for the scope (host-side launch work, seen on
+// the CPU row of nsys and by ncu --nvtx filters). Without a tool attached it costs a check.
+struct TaNvtxRange {
+  explicit TaNvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~TaNvtxRange() { nvtxRangePop(); }
+  TaNvtxRange(const TaNvtxRange&) = delete;
+  TaNvtxRange& operator=(const TaNvtxRange&) = delete;
+};

@@ -66,6 +66,7 @@ extern "C" int ta_sdpa_fwd_split_noalloc(const void* q, const void* k, const voi
                                          const int64_t* v_strides, const int64_t* o_strides,
                                          int dtype, int causal, float scale, int n_split,
                                          unsigned int* dev_status, void* stream) {
+  TaNvtxRange nvtx_range("ta_sdpa_fwd_split_noalloc");
   ta_capi_clear_error();
   if (B <= 0 || H <= 0 || S <= 0 || n_split < 1)
     return ta_capi_fail(TA_ERR_INVALID_ARGUMENT, "B, H, S, n_split must be positive");

@@ -191,6 +191,7 @@ bool aligned16(const void* ptr) { return reinterpret_cast<uintptr_t>(ptr) % 16 =
 extern "C" int ta_peer_barrier(unsigned int* const* flags, int n_peers, int rank,
                                unsigned int epoch, unsigned long long timeout_ns,
                                unsigned int* dev_status, void* stream) {
+  TaNvtxRange nvtx_range("ta_peer_barrier");
   ta_capi_clear_error();
   if (!flags) return ta_capi_fail(TA_ERR_INVALID_ARGUMENT, "null flags array");
   if (n_peers < 1 || n_peers > kMaxPeers || rank < 0 || rank >= n_peers)
@@ -217,6 +218,7 @@ extern "C" int ta_lse_merge_peers(const void* const* o_src, const void* const* l
                                   void* const* o_dst, float* const* lse_dst, int n_dst,
                                   const int64_t* o_strides, int out_rows, int row_base,
                                   int out_dtype, const unsigned int* dev_status, void* stream) {
+  TaNvtxRange nvtx_range("ta_lse_merge_peers");
   ta_capi_clear_error();
   if (!o_src || !lse_src || !o_dst || !o_strides)
     return ta_capi_fail(TA_ERR_INVALID_ARGUMENT, "null pointer argument");
