@@ -1,6 +1,8 @@
 """Host-side multi-rank logic on CPU: pair sharding, zig-zag key slices, the log-sum-exp
 merge, and the merge across ranks over gloo (world size 2), checked against the float64
-oracle; plus failure detection when a rank never joins (no GPU involved)."""
+oracle; plus failure detection on gloo ranks (no GPU involved): a rank that never joins, a
+rank that raises, a rank that arrives after the process-group timeout, and ranks whose
+shards differ in size."""
 
 from __future__ import annotations
 
@@ -157,3 +159,72 @@ def test_row_share_partitions_rows():
                 assert a1 == b0
             sizes = [b - a for a, b in shares]
             assert max(sizes) - min(sizes) <= 1
+
+
+def _fault_worker(rank, world, port, mode, out_q):
+    """Rank 1 misbehaves according to `mode`; rank 0 runs the merge and reports what it saw.
+    Every collective runs under a 3 s process-group timeout, so nothing can hang."""
+    import time
+    from datetime import timedelta
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=3))
+    S = 8
+    if rank == 1 and mode == "raises":
+        out_q.put((rank, "raised"))
+        raise RuntimeError("injected failure on rank 1")  # the process exits non-zero
+    if rank == 1 and mode == "late":
+        time.sleep(6)  # past the others' timeout
+    if rank == 1 and mode == "mismatch":
+        S = 9  # a shard of another size
+    t0 = time.monotonic()
+    try:
+        merge_across_ranks(torch.zeros(2, S, 4), torch.zeros(2, S))
+        res = "no error"
+    except ValueError as exc:
+        res = f"ValueError: {exc}"
+    except Exception as exc:  # a failed collective, not a hang
+        res = f"error: {type(exc).__name__}"
+    out_q.put((rank, res, time.monotonic() - t0))
+    try:
+        dist.destroy_process_group()
+    except Exception:
+        pass
+
+
+def _run_fault(mode):
+    ctx = mp.get_context("spawn")
+    out_q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_fault_worker, args=(r, 2, port, mode, out_q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+        assert p.exitcode is not None, "a rank hung"
+    res = {}
+    while not out_q.empty():
+        item = out_q.get(timeout=10)
+        res[item[0]] = item[1:]
+    return res, [p.exitcode for p in procs]
+
+
+def test_rank_that_raises_is_detected():
+    res, codes = _run_fault("raises")
+    assert res[1] == ("raised",) and codes[1] != 0
+    assert res[0][0].startswith("error"), res[0]
+    assert res[0][1] < 60
+
+
+def test_rank_past_the_timeout_is_detected():
+    res, _ = _run_fault("late")
+    assert res[0][0].startswith("error"), res[0]
+    assert res[0][1] < 60
+
+
+def test_mismatched_shard_sizes_raise_on_every_rank():
+    res, codes = _run_fault("mismatch")
+    for rank in (0, 1):
+        assert res[rank][0].startswith("ValueError"), res[rank]
+        assert "differ in size" in res[rank][0]
+    assert codes == [0, 0]

@@ -73,12 +73,31 @@ def lse_merge(o_parts, lse_parts):
     return o, lse
 
 
-def merge_across_ranks(o_part, lse_part, group=None):
+def merge_across_ranks(o_part, lse_part, group=None, validate: bool | None = None):
     """Collective log-sum-exp merge: every rank passes its fp32 partial (o_part [..., D],
     lse_part [...]) and gets the merged (o, lse) of all ranks. Two collectives: an
-    all-reduce(MAX) of lse and an all-reduce(SUM) of [w*o | w]."""
+    all-reduce(MAX) of lse and an all-reduce(SUM) of [w*o | w].
+
+    validate: first agree on the partials' sizes with one small all-reduce and raise
+    ValueError on every rank if they differ (mismatched shards would otherwise make the
+    collectives fail obscurely or combine unrelated rows). Default: on for host tensors; for
+    device tensors it costs a host synchronisation, so it is opt-in there."""
     import torch
     import torch.distributed as dist
+
+    if validate is None:
+        validate = lse_part.device.type == "cpu"
+    if validate:
+        n, d = lse_part.numel(), int(o_part.shape[-1])
+        sizes = torch.tensor([n, -n, d, -d, o_part.numel(), -o_part.numel()], dtype=torch.int64,
+                             device=lse_part.device)
+        dist.all_reduce(sizes, op=dist.ReduceOp.MAX, group=group)
+        lo_hi = sizes.tolist()
+        if (lo_hi[0] != -lo_hi[1] or lo_hi[2] != -lo_hi[3] or lo_hi[4] != -lo_hi[5]
+                or o_part.numel() != n * d):
+            raise ValueError("merge_across_ranks: the ranks' partial states differ in size "
+                             f"(this rank: lse {tuple(lse_part.shape)}, o "
+                             f"{tuple(o_part.shape)})")
 
     lse_max = lse_part.clone()
     dist.all_reduce(lse_max, op=dist.ReduceOp.MAX, group=group)
