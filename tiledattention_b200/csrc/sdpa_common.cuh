@@ -46,28 +46,31 @@ struct Item {
   int split, bh, b, h, q_row0, kv_lo, kv_hi, n_kv;
 };
 
+__host__ __device__ __forceinline__ int imin(int a, int b) { return a < b ? a : b; }
+
 // Item order: key slice, then groups of group_bh (b,h) pairs whose K/V fit in L2 together;
 // inside a group the longest causal query blocks (of kRows rows) of all its pairs come
 // first, pairs interleaved, so the dynamic scheduler ends each group, and the launch, on
-// short items.
+// short items. Host-callable too, so the order is checked on the CPU
+// (tests/native/decode_item_check.cu).
 template <bool CAUSAL, int kRows, int kKeysPerTile>
-__device__ __forceinline__ Item decode_item(const FwdParams& p, int item) {
+__host__ __device__ __forceinline__ Item decode_item(const FwdParams& p, int item) {
   Item it;
   const int per_split = p.BH * p.n_qblk;
   it.split = item / per_split;
   const int rem = item - it.split * per_split;
   const int group = rem / (p.group_bh * p.n_qblk);
   const int within = rem - group * (p.group_bh * p.n_qblk);
-  const int gsize = min(p.group_bh, p.BH - group * p.group_bh);
+  const int gsize = imin(p.group_bh, p.BH - group * p.group_bh);
   const int qblk = p.n_qblk - 1 - within / gsize;
   it.bh = group * p.group_bh + within % gsize;
   it.b = it.bh / p.H;
   it.h = it.bh % p.H;
   it.q_row0 = qblk * kRows;
   // keys [kv_lo, kv_hi) take part (the whole range, or one slice for split-KV)
-  it.kv_lo = min(p.kv_end, p.kv_begin + it.split * p.split_len);
-  it.kv_hi = min(p.kv_end, it.kv_lo + p.split_len);
-  const int kv_rows = CAUSAL ? min(it.kv_hi, it.q_row0 + kRows) : it.kv_hi;
+  it.kv_lo = imin(p.kv_end, p.kv_begin + it.split * p.split_len);
+  it.kv_hi = imin(p.kv_end, it.kv_lo + p.split_len);
+  const int kv_rows = CAUSAL ? imin(it.kv_hi, it.q_row0 + kRows) : it.kv_hi;
   it.n_kv = kv_rows > it.kv_lo ? (kv_rows - it.kv_lo + kKeysPerTile - 1) / kKeysPerTile : 0;
   return it;
 }
