@@ -18,11 +18,22 @@ Fields beyond the base contract:
   roofline  tensor-bound: algorithmic FLOP per launch / average launch time vs the
             measured bf16 peak (MEASURED_PEAKS.json), traffic from the committed ncu
             summary (profiles/)
-  cpu_baseline  the C oracle (float32 build, all host threads) on a bounded sample of
-            the same workload (rank 0, N=1 only)
-  --impl reference  times the reference's CPU path stand-in: the reference has no CPU
-            implementation (its sdpa rejects non-CUDA tensors), so the arm runs the
-            oracle port of its algorithm on all host threads, on a bounded sample.
+  max_abs_err  the last timed step's output checked, after the timed region, against the
+            float64 oracle on sampled query-row blocks of sampled (b,h) pairs (max over
+            ranks), with the tolerance it must meet
+  sustained a seconds-long loop of the same step after the timed region, with its own
+            clock record, judged against the sustained bf16 peak (bf16_tflops_sustained)
+  ranks     (N > 1) each rank's step-time median / min / max, its kernel time, SM clock
+            median and GPU utilisation during the timed region, and how many were busy
+  context   torch's own GPU SDPA (scaled_dot_product_attention, default backend choice)
+            on the same inputs, timed the same way (N = 1): a same-box comparison only
+  cpu_baseline  the reference's CPU path as north_star names it: torch SDPA math backend
+            in float32 on all host threads, on a bounded sample of the same workload
+            (rank 0, N=1 only); the C oracle port's rate on the same sample is reported
+            beside it ("port")
+  --impl reference  times that same CPU path (torch SDPA math, float32, all host threads):
+            the reference has no CPU implementation of its own (its sdpa rejects non-CUDA
+            tensors) and its cuTile GPU kernel cannot run on this image.
 """
 
 from __future__ import annotations
@@ -81,8 +92,26 @@ def ncu_traffic_per_launch():
     return float(m.group(1)) if m else None
 
 
+def _nvml_handle(torch, device):
+    """NVML handle of a torch CUDA device, matched by PCI address (CUDA_VISIBLE_DEVICES may
+    renumber devices), falling back to the same index; (None, None) without NVML."""
+    try:
+        import pynvml
+
+        pynvml.nvmlInit()
+        try:
+            pr = torch.cuda.get_device_properties(device)
+            bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(device.index or 0)
+    except Exception:
+        return None, None
+
+
 class ClockSampler:
-    """Samples SM clock and throttle reasons through NVML (read-only) in a thread."""
+    """Samples SM clock, GPU utilisation and throttle reasons through NVML (read-only) in a
+    thread."""
 
     REASONS = {
         "hw_slowdown": 0x8,
@@ -91,34 +120,36 @@ class ClockSampler:
         "sw_power_cap": 0x4,
     }
 
-    def __init__(self, device_index, period_s=0.02):
+    def __init__(self, torch, device, period_s=0.02):
         self.samples = []
+        self.util = []
         self.reasons = set()
         self.max_mhz = None
         self.period = period_s
         self._stop = threading.Event()
         self._thread = None
-        try:
-            import pynvml
+        self._nvml, self._h = _nvml_handle(torch, device)
+        if self._nvml is not None:
+            try:
+                self.max_mhz = self._nvml.nvmlDeviceGetMaxClockInfo(self._h, self._nvml.NVML_CLOCK_SM)
+            except Exception:
+                self._nvml = None
 
-            pynvml.nvmlInit()
-            self._nvml = pynvml
-            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
-            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+    def _sample(self):
+        nv = self._nvml
+        try:
+            self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+            self.util.append(nv.nvmlDeviceGetUtilizationRates(self._h).gpu)
+            mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+            for name, bit in self.REASONS.items():
+                if mask & bit:
+                    self.reasons.add(name)
         except Exception:
-            self._nvml = None
+            pass
 
     def _run(self):
-        nv = self._nvml
         while not self._stop.is_set():
-            try:
-                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
-                mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
-                for name, bit in self.REASONS.items():
-                    if mask & bit:
-                        self.reasons.add(name)
-            except Exception:
-                pass
+            self._sample()
             time.sleep(self.period)
 
     def start(self):
@@ -130,12 +161,17 @@ class ClockSampler:
         if self._thread is not None:
             self._stop.set()
             self._thread.join()
+            if len(self.samples) < 2:  # a run shorter than the period: one more sample
+                self._sample()
         return {
             "sm_mhz": statistics.median(self.samples) if self.samples else None,
             "sm_max_mhz": self.max_mhz,
             "reasons": sorted(self.reasons),
             "samples": len(self.samples),
         }
+
+    def util_median(self):
+        return statistics.median(self.util) if self.util else None
 
 
 def make_inputs(torch, pairs, S, D, dtype, pair_start, device=None, pinned=False):
@@ -154,27 +190,66 @@ def make_inputs(torch, pairs, S, D, dtype, pair_start, device=None, pinned=False
     return q, k, v
 
 
-def cpu_sample(S, D, causal, target_s):
-    """Time the C oracle (float32, all host threads) on whole (b,h) pairs of the workload,
-    growing the number of pairs until about target_s seconds. Returns (tflops, desc, cores)."""
+def _cpu_pairs(pairs, S, D):
     import numpy as np
 
-    from oracle import oracle
-
     rng = np.random.default_rng(SEED)
-    cores = oracle.oracle_threads()
+    return [rng.standard_normal((1, pairs, S, D), dtype=np.float32) for _ in range(3)]
+
+
+def cpu_sample_torch_math(S, D, causal, target_s):
+    """The reference's CPU path as its benchmarks define it (torch SDPA, math backend,
+    float32; benchmark-gb10/run_study.py:249-271) on all host threads, over whole (b,h)
+    pairs of the workload, growing the number of pairs until about target_s seconds.
+    Returns (tflops, desc, cores, seconds, pairs)."""
+    import torch
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
     pairs = 1
     while True:
-        q, k, v = (rng.standard_normal((1, pairs, S, D), dtype=np.float32) for _ in range(3))
+        q, k, v = (torch.from_numpy(a) for a in _cpu_pairs(pairs, S, D))
         t0 = time.perf_counter()
-        oracle.sdpa_c(q, k, v, causal=causal, scale=1.0 / math.sqrt(D), precision="f32")
+        with sdpa_kernel(SDPBackend.MATH):
+            for i in range(pairs):  # one pair at a time: the S x S score matrix stays small
+                torch.nn.functional.scaled_dot_product_attention(
+                    q[:, i:i + 1], k[:, i:i + 1], v[:, i:i + 1], is_causal=causal,
+                    scale=1.0 / math.sqrt(D))
         dt = time.perf_counter() - t0
         if dt >= target_s * 0.5 or pairs >= 256:
             break
         pairs = min(256, max(pairs + 1, int(pairs * target_s / max(dt, 1e-3))))
     tflops = flops(1, pairs, S, D, causal) / dt / 1e12
-    desc = f"{pairs} of 256 (b,h) pairs at S={S} D={D} causal={causal}, float32 C oracle, {dt:.2f} s"
-    return tflops, desc, cores, dt
+    desc = (f"{pairs} of 256 (b,h) pairs at S={S} D={D} causal={causal}, torch "
+            f"{torch.__version__} scaled_dot_product_attention math backend, float32, "
+            f"{cores} threads, {dt:.2f} s")
+    return tflops, desc, cores, dt, pairs
+
+
+def cpu_sample_port(S, D, causal, pairs):
+    """The float32 C oracle port (all host threads) on the same pairs. Returns
+    (tflops, desc, cores)."""
+    from oracle import oracle
+
+    q, k, v = _cpu_pairs(pairs, S, D)
+    cores = oracle.oracle_threads()
+    t0 = time.perf_counter()
+    oracle.sdpa_c(q, k, v, causal=causal, scale=1.0 / math.sqrt(D), precision="f32")
+    dt = time.perf_counter() - t0
+    return (flops(1, pairs, S, D, causal) / dt / 1e12,
+            f"{pairs} (b,h) pairs, float32 C oracle port, {cores} threads, {dt:.2f} s", cores)
+
+
+def _cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
 
 
 def run_reference_arm(args, rank, world):
@@ -186,11 +261,11 @@ def run_reference_arm(args, rank, world):
     default_step = min(2.0, max(0.2, 120.0 / (args.steps + 0.25 * args.warmup)))
     per_step = max(0.1, float(os.environ.get("TA_REF_STEP_S", str(default_step))))
     for _ in range(args.warmup):
-        cpu_sample(wl["S"], wl["D"], wl["causal"], per_step / 4)
+        cpu_sample_torch_math(wl["S"], wl["D"], wl["causal"], per_step / 4)
     vals, descs, total = [], [], 0.0
     cores = None
     for _ in range(args.steps):
-        v, d, cores, dt = cpu_sample(wl["S"], wl["D"], wl["causal"], per_step)
+        v, d, cores, dt, _ = cpu_sample_torch_math(wl["S"], wl["D"], wl["causal"], per_step)
         vals.append(v)
         descs.append(d)
         total += dt
@@ -212,15 +287,34 @@ def run_reference_arm(args, rank, world):
         "config": {"workload": wl["name"], "B": wl["B"], "H": wl["H"], "S": wl["S"],
                    "D": wl["D"], "causal": wl["causal"], "sample": descs[-1]},
         "cpu_baseline": {"value": round(value, 5), "unit": "TFLOP/s", "cores": cores,
-                         "kind": "port", "sample": descs[-1]},
+                         "kind": "reference", "sample": descs[-1], "cpu": _cpu_model()},
         "e2e": {"value": round(value, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
-        "note": "the reference has no CPU implementation (sdpa rejects non-CUDA tensors, "
-                "src/tiledattention/utils/checks.py:42-43); its cuTile GPU kernel needs cupy "
-                "and tileiras (CUDA 13.1), absent from this image. This arm times the C port "
-                "of its algorithm (oracle/sdpa_oracle.c, float32) on all host threads.",
+        "note": "the reference's CPU path as north_star defines it: torch SDPA math backend in "
+                "float32 on all host threads (the reference's own sdpa rejects non-CUDA tensors, "
+                "src/tiledattention/utils/checks.py:42-43, and its cuTile GPU kernel needs cupy "
+                "and tileiras (CUDA 13.1), absent from this image).",
     }
     print(json.dumps(line), flush=True)
+
+
+def self_check(torch, o, q, k, v, causal, world):
+    """Max-abs error of the step's output against the float64 oracle on the first and last
+    128-row block of the first, middle and last (b,h) pair of this rank's shard (outside the
+    timed region). Returns (max error over ranks, description)."""
+    import numpy as np
+
+    from oracle import oracle
+
+    pairs, S, D = q.shape[1], q.shape[2], q.shape[3]
+    idx = sorted({0, pairs // 2, pairs - 1})
+    blocks = [(0, min(S, 128)), (max(0, S - 128), S)]
+    qs, ks, vs, os_ = (t[:, idx].float().cpu() for t in (q, k, v, o))
+    err = 0.0
+    for r0, r1 in blocks:
+        ref = oracle.sdpa_c(qs, ks, vs, causal=causal, scale=1.0 / math.sqrt(D), rows=(r0, r1))
+        err = max(err, float(np.abs(os_[:, :, r0:r1].numpy() - ref[:, :, r0:r1]).max()))
+    return err, f"rows {blocks} of pairs {idx} of each rank's shard vs the float64 oracle"
 
 
 def main():
@@ -231,6 +325,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sustained-s", type=float, default=4.0,
+                    help="length of the sustained-regime loop after the timed region (0: skip)")
+    ap.add_argument("--no-context", action="store_true",
+                    help="skip timing torch's own GPU SDPA on the same inputs")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="llama_prefill")
     ap.add_argument("--mode", choices=["bh", "split_kv"], default="bh",
                     help="bh: shard (batch, head) pairs over ranks, no collective; split_kv: "
@@ -241,7 +339,7 @@ def main():
                          "(collective) or over NVLink peer memory with this package's barrier "
                          "and merge kernels (peer)")
     ap.add_argument("--pairs", type=int, default=0,
-                    help="profiling case: run only this many of the 256 (b,h) pairs")
+                    help="profiling case: run only this many of the (b,h) pairs")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
@@ -301,32 +399,90 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    sampler = ClockSampler(device.index if device.index is not None else 0)
+    def timed_loop(n, fn):
+        """n steps, each after an (untimed) L2 flush; per-step device times in ms."""
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+        out = None
+        for i in range(n):
+            flush.zero_()  # L2 flush, enqueued before the start event: not timed
+            starts[i].record(stream)
+            out = fn(q, k, v)
+            ends[i].record(stream)
+        torch.cuda.synchronize(device)
+        return [s_.elapsed_time(e_) for s_, e_ in zip(starts, ends)], out
+
+    sampler = ClockSampler(torch, device)
     for _ in range(args.warmup):
         flush.zero_()
         o = step_fn(q, k, v)
     torch.cuda.synchronize(device)
     ta.check_device_status(device)
 
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     sampler.start()
     barrier()
     torch.cuda.synchronize(device)
-    for i in range(args.steps):
-        flush.zero_()  # L2 flush, enqueued before the start event: not timed
-        starts[i].record(stream)
-        o = step_fn(q, k, v)
-        ends[i].record(stream)
-    torch.cuda.synchronize(device)
+    step_ms, o = timed_loop(args.steps, step_fn)
     barrier()
     clocks = sampler.stop()
     ta.check_device_status(device)
-    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     total_ms = max_over_ranks(sum(step_ms))
     avg_launch_ms = sum(step_ms) / len(step_ms)
     value = job_flops * args.steps / (total_ms / 1e3) / 1e12
+
+    # ---- correctness of what was timed (outside the timed region)
+    tol = 1e-2  # bfloat16 max-abs bound of north_star
+    err = max_over_ranks(self_check(torch, o, q, k, v, causal, world)[0])
+    check_desc = self_check.__doc__.split("(")[0].strip()
     del o
+
+    # ---- per-rank record (N > 1): where the time goes on each GPU
+    ranks = None
+    if world > 1:
+        mine = {"rank": rank, "pairs": pairs,
+                "step_ms_median": round(statistics.median(step_ms), 4),
+                "step_ms_min": round(min(step_ms), 4), "step_ms_max": round(max(step_ms), 4),
+                "sm_mhz": clocks["sm_mhz"], "gpu_util_median": sampler.util_median(),
+                "reasons": clocks["reasons"]}
+        gathered = [None] * world
+        dist.all_gather_object(gathered, mine)
+        ranks = {"per_rank": gathered,
+                 "gpus_busy": sum(1 for r in gathered if (r["gpu_util_median"] or 0) > 0),
+                 "step_ms_spread": round(max(r["step_ms_median"] for r in gathered) -
+                                         min(r["step_ms_median"] for r in gathered), 4)}
+
+    # ---- sustained regime: several seconds of the same step, with its own clock record
+    sustained = None
+    if args.sustained_s > 0:
+        n_sus = max(200, int(args.sustained_s * 1000 / max(avg_launch_ms + 0.05, 1e-3)))
+        sus_sampler = ClockSampler(torch, device)
+        sus_sampler.start()
+        barrier()
+        sus_ms, o = timed_loop(n_sus, step_fn)
+        barrier()
+        sus_clocks = sus_sampler.stop()
+        del o
+        sus_total = max_over_ranks(sum(sus_ms))
+        sus_value = job_flops * n_sus / (sus_total / 1e3) / 1e12
+        sustained = {"value": round(sus_value, 2), "steps": n_sus,
+                     "seconds": round(sus_total / 1e3, 2), "clocks": sus_clocks}
+
+    # ---- same-box context: torch's own GPU SDPA on the same inputs, timed the same way
+    context = None
+    if world == 1 and not args.no_context and args.mode == "bh":
+        try:
+            def torch_sdpa(q_, k_, v_):
+                return torch.nn.functional.scaled_dot_product_attention(q_, k_, v_, is_causal=causal)
+
+            for _ in range(3):
+                torch_sdpa(q, k, v)
+            t_ms, o = timed_loop(max(5, min(args.steps, 50)), torch_sdpa)
+            del o
+            context = {"torch_sdpa_gpu_tflops": round(step_flops * len(t_ms) / (sum(t_ms) / 1e3) / 1e12, 2),
+                       "what": f"torch {torch.__version__} F.scaled_dot_product_attention "
+                               "(default backend choice) on the same inputs, same flush/timing"}
+        except Exception as exc:  # context only: never fails the bench
+            context = {"error": repr(exc)[:200]}
 
     # ---- end to end through the public API, host buffers, copies inside the timing.
     # Every step copies its q, k, v host->device and its o device->host. The copies run
@@ -397,15 +553,22 @@ def main():
 
     peaks, peak_kind = measured_peaks()
     peak = float(peaks.get("bf16_tflops", FALLBACK_PEAK_TFLOPS))
+    peak_sus = float(peaks.get("bf16_tflops_sustained", peak))
     achieved = step_flops / (avg_launch_ms / 1e3) / 1e12
     traffic = (ncu_traffic_per_launch()
                if world == 1 and args.workload == "llama_prefill" and args.mode == "bh" else None)
+    if sustained is not None:
+        sustained["frac_of_sustained_peak"] = round(sustained["value"] / world / peak_sus, 4)
+        sustained["peak_sustained"] = peak_sus
 
     cpu = None
     if world == 1 and not args.no_cpu_baseline and args.workload == "llama_prefill":
-        v_cpu, desc, cores, _ = cpu_sample(S, D, causal, float(os.environ.get("TA_CPU_SAMPLE_S", "10")))
-        cpu = {"value": round(v_cpu, 5), "unit": "TFLOP/s", "cores": cores, "kind": "port",
-               "sample": desc}
+        v_cpu, desc, cores, _, cpu_pairs = cpu_sample_torch_math(
+            S, D, causal, float(os.environ.get("TA_CPU_SAMPLE_S", "10")))
+        v_port, desc_port, cores_port = cpu_sample_port(S, D, causal, cpu_pairs)
+        cpu = {"value": round(v_cpu, 5), "unit": "TFLOP/s", "cores": cores, "kind": "reference",
+               "sample": desc, "cpu": _cpu_model(),
+               "port": {"value": round(v_port, 5), "cores": cores_port, "sample": desc_port}}
 
     line = {
         "metric": "sdpa_fwd_tflops",
@@ -427,6 +590,7 @@ def main():
                    **({"exchange": args.exchange} if args.mode == "split_kv" and world > 1 else {}),
                    "l2": "256 MB L2 flush enqueued before every timed step",
                    "pct_of_bf16_peak": round(100 * value / world / peak, 2)},
+        "max_abs_err": {"value": err, "tol": tol, "pass": bool(err <= tol), "what": check_desc},
         "e2e": {"value": round(e2e_value, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e_steps,
                 "path": "pinned host q,k,v -> H2D (two copy streams) -> tiledattention_b200 call -> "
@@ -434,11 +598,13 @@ def main():
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak,
                      "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
                      "peak_source": f"{peak_kind} bf16_tflops (burst)",
-                     "frac_of_sustained_peak": round(
-                         achieved / float(peaks.get("bf16_tflops_sustained", peak)), 4),
+                     "frac_of_sustained_peak": round(achieved / peak_sus, 4),
                      "traffic": traffic},
+        "sustained": sustained,
         "cpu_baseline": cpu,
         "clocks": clocks,
+        "ranks": ranks,
+        "context": context,
         # per rank and step: bh 1 forward; split_kv on one GPU forward + combine; at N>1 two
         # zig-zag partial forwards + combine (collective) or + barrier, merge, barrier (peer)
         "gpu_launches": args.steps * world * (

@@ -22,9 +22,10 @@
  * Layout: q, k, v, o are 4-D [B, H, S, D] tensors given by a base pointer and four
  * element strides (batch, head, sequence, dim). The dim stride must be 1; the other
  * strides times the element size must be multiples of 16 bytes and the base pointers
- * 16-byte aligned (TMA descriptor rules). Supported head dims: 64, 128, 256 (other head
- * dims are zero-padded to the next one by the Python launcher, as the reference pads to
- * the next power of two, flash_fwd.py:149-163).
+ * 16-byte aligned (TMA descriptor rules). Supported head dims: every multiple of 8 up to
+ * 256 (64, 128 and 256 natively, the others on the next native kernel without padded
+ * copies); other head dims up to 256 are zero-padded by the Python launcher, where the
+ * reference pads to the next power of two (flash_fwd.py:149-163).
  */
 #ifndef TILEDATTENTION_B200_H
 #define TILEDATTENTION_B200_H
@@ -200,15 +201,6 @@ const char* ta_last_error(void);
  * Call ta_debug_set_selftest(0, 0) to restore normal operation. No reference counterpart.
  */
 void ta_debug_set_selftest(int stall, unsigned long long timeout_ns);
-
-/*
- * ta_debug_set_cta_pair — process-wide switch (off by default) that runs head-dim-128 work
- * below the shared-K/V crossover on the CTA-pair kernel: 2-CTA clusters issuing
- * tcgen05 cta_group::2 MMAs over 256-row items, each CTA loading half of every K/V tile.
- * Same results (parity-tested); measured ~7 % slower than the default single-CTA kernel on
- * B200, kept for experiments. No reference counterpart.
- */
-void ta_debug_set_cta_pair(int on);
 
 /* ta_abi_version — ABI version of this library (major*100 + minor). */
 int ta_abi_version(void);

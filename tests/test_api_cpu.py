@@ -216,3 +216,17 @@ def test_state_head_dim_policy():
         8, 64, 96, 128, 128, 160, 200, 248, 256, 64]
     with pytest.raises(InvalidShapeError):
         state_head_dim(257)
+
+
+@pytest.mark.parametrize("bad", ["strcit", "sync", "POSTT"])
+def test_unknown_sync_mode_raises(monkeypatch, bad):
+    """An unknown TILEDATTN_SYNC_MODE raises the reference's ValueError
+    (flash_fwd.py:814-818) instead of silently running asynchronously."""
+    from tiledattention_b200 import launch
+
+    monkeypatch.setenv("TILEDATTN_SYNC_MODE", bad)
+    with pytest.raises(ValueError, match="Unsupported TILEDATTN_SYNC_MODE"):
+        launch._sync_mode()
+    for good in ("async", " Post ", "STRICT"):
+        monkeypatch.setenv("TILEDATTN_SYNC_MODE", good)
+        assert launch._sync_mode() == good.strip().lower()

@@ -5,7 +5,9 @@ cuTile JIT + compile cache, src/tiledattention/kernels/compile_cache.py:10-37).
 
 compiles csrc/*.cu with nvcc for sm_100a into _lib/libtiledattention_b200.so
 (in-tree, so the built library travels with the source tree). Every variant
-(head dim 64/128 x fp16/bf16 x causal/non-causal) is instantiated at build time.
+(kernel head dim 64/128/256 x fp16/bf16 x causal/non-causal x 16-bit/fp32-partial output)
+is instantiated at build time; any head dim that is a multiple of 8 up to 256 runs on the
+next kernel head dim without padded copies.
 """
 
 from __future__ import annotations
@@ -20,8 +22,8 @@ REPO_DIR = os.path.dirname(PKG_DIR)
 CSRC = os.path.join(PKG_DIR, "csrc")
 OUT_DIR = os.path.join(PKG_DIR, "_lib")
 OUT = os.path.join(OUT_DIR, "libtiledattention_b200.so")
-SOURCES = ["capi.cu", "sdpa_fwd_sm100.cu", "sdpa_fwd_sm100_shared_kv.cu", "sdpa_fwd_sm100_pair.cu", "lse_combine.cu", "noalloc_split.cu", "peer_merge.cu"]
-HEADERS = ["sm100_ptx.cuh", "sm100_pair.cuh", "sdpa_common.cuh", "sdpa_fwd_sm100.h", "lse_combine.h", "capi_internal.h"]
+SOURCES = ["capi.cu", "sdpa_fwd_sm100.cu", "sdpa_fwd_sm100_shared_kv.cu", "lse_combine.cu", "noalloc_split.cu", "peer_merge.cu"]
+HEADERS = ["sm100_ptx.cuh", "sdpa_common.cuh", "sdpa_fwd_sm100.h", "lse_combine.h", "capi_internal.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 # One-call host launcher (CPython extension over libtorch; no device code): see
 # csrc/fast_launch.cpp.

@@ -107,8 +107,6 @@ int check_device() {
 #ifdef TA_TRACE
 unsigned long long* g_trace = nullptr;
 #endif
-// Experimental CTA-pair kernel switch (ta_debug_set_cta_pair); off by default.
-std::atomic<int> g_cta_pair{0};
 // Failure-path self-test settings (ta_debug_set_selftest); off by default.
 std::atomic<int> g_selftest_stall{0};
 std::atomic<unsigned long long> g_timeout_ns{0};
@@ -116,9 +114,6 @@ std::atomic<unsigned long long> g_timeout_ns{0};
 
 int ta_capi_fail(int code, const char* msg) { return fail(code, "%s", msg); }
 
-namespace ta {
-bool cta_pair_requested() { return g_cta_pair.load(std::memory_order_relaxed) != 0; }
-}  // namespace ta
 void ta_capi_clear_error() { g_last_error.clear(); }
 
 extern "C" {
@@ -136,7 +131,6 @@ void ta_debug_set_selftest(int stall, unsigned long long timeout_ns) {
   g_timeout_ns.store(timeout_ns);
 }
 
-void ta_debug_set_cta_pair(int on) { g_cta_pair.store(on ? 1 : 0); }
 
 const char* ta_last_error(void) { return g_last_error.c_str(); }
 
@@ -144,7 +138,7 @@ const char* ta_status_string(int status) {
   switch (status) {
     case TA_OK: return "ok";
     case TA_ERR_INVALID_ARGUMENT: return "invalid argument";
-    case TA_ERR_UNSUPPORTED_DIM: return "unsupported head dim (supported: 64, 128, 256)";
+    case TA_ERR_UNSUPPORTED_DIM: return "unsupported head dim (supported: multiples of 8 up to 256)";
     case TA_ERR_UNSUPPORTED_DTYPE: return "unsupported dtype (supported: float16, bfloat16)";
     case TA_ERR_LAYOUT: return "layout not expressible as a TMA tensor map";
     case TA_ERR_CUDA: return "CUDA runtime error";
@@ -216,11 +210,6 @@ int run_forward(const void* q, const void* k, const void* v, void* o, bool out_f
   if (!out_f32 && !ta::uses_shared_kv(kd, S, causal != 0) &&
       (rc = make_map(&mo, o, B, H, S, D, o_strides, dtype, "o")))
     return rc;
-  CUtensorMap mk64;
-  memset(&mk64, 0, sizeof(mk64));
-  if (ta::uses_pair(kd, S, causal != 0) &&
-      (rc = make_map(&mk64, k, B, H, S, D, k_strides, dtype, "k", 64)))
-    return rc;
 
   ta::FwdParams p{};
   p.o = o;
@@ -249,7 +238,7 @@ int run_forward(const void* q, const void* k, const void* v, void* o, bool out_f
 #endif
   p.timeout_ns = g_timeout_ns.load();
   p.selftest_stall = g_selftest_stall.load();
-  cudaError_t err = ta::launch_sdpa_fwd(mq, mk, mv, mo, mk64, p, kd, dtype == TA_DTYPE_BF16,
+  cudaError_t err = ta::launch_sdpa_fwd(mq, mk, mv, mo, p, kd, dtype == TA_DTYPE_BF16,
                                         causal != 0, out_f32, static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess)
     return fail(TA_ERR_CUDA, "kernel launch failed: %s", cudaGetErrorString(err));

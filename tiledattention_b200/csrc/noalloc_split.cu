@@ -11,8 +11,9 @@
 // Costs and limits of that choice:
 //   - every GPU that loads the library reserves kScratchBytes (64 MiB) of global memory
 //     for this array until the process exits, whether or not this entry point is used;
-//   - one call needs n_split * B * H * S * (Dk + 1) * 4 bytes of it (Dk = 64 or 128, the
-//     kernel head dim); larger problems are rejected with TA_ERR_INVALID_ARGUMENT;
+//   - one call needs n_split * B * H * S * (D + 1) * 4 bytes of it (D = the caller's head
+//     dim, a multiple of 8 up to 256); larger problems are rejected with
+//     TA_ERR_INVALID_ARGUMENT;
 //   - all calls on a device share the one array, so calls whose work overlaps on the GPU
 //     (different streams, or different host threads without ordering) race and corrupt
 //     each other's results. Issue them on one stream, or order them. Each call overwrites

@@ -784,12 +784,10 @@ std::atomic<int> g_sm_count[kMaxDevices];
 }  // namespace
 
 cudaError_t launch_sdpa_fwd(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
-                            const CUtensorMap& o, const CUtensorMap& k64, const FwdParams& p_in,
+                            const CUtensorMap& o, const FwdParams& p_in,
                             int D, bool bf16, bool causal, bool out_f32, cudaStream_t stream) {
   if (uses_shared_kv(D, p_in.S, causal))
     return launch_sdpa_fwd_shared_kv(q, k, v, p_in, D, bf16, causal, out_f32, stream);
-  if (uses_pair(D, p_in.S, causal))
-    return launch_sdpa_fwd_pair(q, k64, v, o, p_in, D, bf16, causal, out_f32, stream);
   const long long items = static_cast<long long>(p_in.n_split) * p_in.BH * p_in.n_qblk;
   if (items == 0) return cudaSuccess;
   if (items > 0x7fffffffll) return cudaErrorInvalidValue;
@@ -838,7 +836,7 @@ cudaError_t launch_sdpa_fwd(const CUtensorMap& q, const CUtensorMap& k, const CU
 
 int rows_per_cta(int D, int S, bool causal) {
   if (uses_shared_kv(D, S, causal)) return rows_per_cta_shared_kv(D);
-  return uses_pair(D, S, causal) ? 2 * kRowsPerTile : kRowsPerTile;
+  return kRowsPerTile;
 }
 
 }  // namespace ta

@@ -44,22 +44,6 @@ inline bool uses_shared_kv(int D, int S, bool causal) {
          (D == 128 && S >= (causal ? kSharedKvMinSeq : kSharedKvMinSeqNonCausal));
 }
 
-// Whether head-dim-128 work below the shared-K/V crossover runs on CTA pairs
-// (sdpa_fwd_sm100_pair.cu: 256-row items, cta_group::2 MMAs) instead of single CTAs. Off by
-// default: measured ~7 % slower on B200 (config 3: 979 vs 1049 TFLOP/s), see the design notes.
-#ifndef TA_USE_PAIR
-#define TA_USE_PAIR 0
-#endif
-bool cta_pair_requested();  // runtime switch (ta_debug_set_cta_pair), off by default
-inline bool uses_pair(int D, int S, bool causal) {
-  return (TA_USE_PAIR || cta_pair_requested()) && D == 128 && !uses_shared_kv(D, S, causal);
-}
-
-// The CTA-pair kernel; k64 maps K with a 64 x 64 box (each CTA loads half a key tile).
-cudaError_t launch_sdpa_fwd_pair(const CUtensorMap& q, const CUtensorMap& k64,
-                                 const CUtensorMap& v, const CUtensorMap& o, const FwdParams& p,
-                                 int D, bool bf16, bool causal, bool out_f32, cudaStream_t stream);
-
 // Query rows one CTA (one work item of the persistent kernel) covers for (D, S, causal).
 int rows_per_cta(int D, int S, bool causal);
 
@@ -71,10 +55,9 @@ int rows_per_cta_shared_kv(int D);
 
 // Launches the variant for (D, dtype, causal) on `stream`. Tensor maps are 4-D
 // (D, S, H, B) with a 64 x 128 box and 128-byte swizzle.
-// `o` is a map of the output like q's (used for 16-bit output; ignored when out_f32);
-// `k64` maps K with a 64 x 64 box (used by the CTA-pair kernel only).
+// `o` is a map of the output like q's (used for 16-bit output; ignored when out_f32).
 cudaError_t launch_sdpa_fwd(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
-                            const CUtensorMap& o, const CUtensorMap& k64, const FwdParams& p,
+                            const CUtensorMap& o, const FwdParams& p,
                             int D, bool bf16, bool causal, bool out_f32, cudaStream_t stream);
 
 }  // namespace ta

@@ -99,8 +99,13 @@ def _tma_compatible(t) -> bool:
 
 
 def _sync_mode() -> str:
+    """TILEDATTN_SYNC_MODE, as the reference reads it (flash_fwd.py:805-818): an unknown
+    value raises the reference's ValueError instead of silently running asynchronously."""
     mode = os.getenv("TILEDATTN_SYNC_MODE", "async").strip().lower()
-    return mode if mode in ("async", "post", "strict") else "async"
+    if mode not in ("async", "post", "strict"):
+        raise ValueError(
+            f"Unsupported TILEDATTN_SYNC_MODE={mode!r}. Use one of: strict, post, async.")
+    return mode
 
 
 def run_sdpa_fwd(q, k, v, *, causal: bool, scale: float, return_lse: bool = False):
