@@ -100,6 +100,7 @@ SIGNATURES = {
     "ta_last_error": (ctypes.c_char_p, []),
     "ta_abi_version": (ctypes.c_int, []),
     "ta_debug_set_selftest": (None, [ctypes.c_int, ctypes.c_ulonglong]),
+    "ta_debug_set_kernel": (None, [ctypes.c_int]),
 }
 
 _lib = None

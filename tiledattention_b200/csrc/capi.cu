@@ -148,6 +148,8 @@ const char* ta_status_string(int status) {
   }
 }
 
+void ta_debug_set_kernel(int kind) { ta::force_kernel(kind); }
+
 int ta_device_supported(int device) {
   int major = 0, minor = 0;
   if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device) != cudaSuccess)
@@ -205,9 +207,11 @@ int run_forward(const void* q, const void* k, const void* v, void* o, bool out_f
   if ((rc = make_map(&mq, q, B, H, S, D, q_strides, dtype, "q"))) return rc;
   if ((rc = make_map(&mk, k, B, H, S, D, k_strides, dtype, "k"))) return rc;
   if ((rc = make_map(&mv, v, B, H, S, D, v_strides, dtype, "v"))) return rc;
+  const ta::KernelKind kind =
+      ta::select_kernel(kd, S, causal != 0, static_cast<long long>(B) * H);
   CUtensorMap mo;
   memset(&mo, 0, sizeof(mo));
-  if (!out_f32 && !ta::uses_shared_kv(kd, S, causal != 0) &&
+  if (!out_f32 && kind == ta::kPersistent &&
       (rc = make_map(&mo, o, B, H, S, D, o_strides, dtype, "o")))
     return rc;
 
@@ -230,7 +234,7 @@ int run_forward(const void* q, const void* k, const void* v, void* o, bool out_f
   const int span = kv_end - kv_begin;
   p.split_len = ((span + n_split - 1) / n_split + 127) / 128 * 128;
   if (p.split_len == 0) p.split_len = 128;
-  const int rows_per_item = ta::rows_per_cta(kd, S, causal != 0);
+  const int rows_per_item = ta::rows_per_item(kind, kd);
   p.n_qblk = (S + rows_per_item - 1) / rows_per_item;
   p.scale_log2 = static_cast<float>(static_cast<double>(scale) * 1.4426950408889634);
 #ifdef TA_TRACE
@@ -239,7 +243,8 @@ int run_forward(const void* q, const void* k, const void* v, void* o, bool out_f
   p.timeout_ns = g_timeout_ns.load();
   p.selftest_stall = g_selftest_stall.load();
   cudaError_t err = ta::launch_sdpa_fwd(mq, mk, mv, mo, p, kd, dtype == TA_DTYPE_BF16,
-                                        causal != 0, out_f32, static_cast<cudaStream_t>(stream));
+                                        causal != 0, out_f32, kind,
+                                        static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess)
     return fail(TA_ERR_CUDA, "kernel launch failed: %s", cudaGetErrorString(err));
   return TA_OK;

@@ -44,8 +44,28 @@ inline bool uses_shared_kv(int D, int S, bool causal) {
          (D == 128 && S >= (causal ? kSharedKvMinSeq : kSharedKvMinSeqNonCausal));
 }
 
-// Query rows one CTA (one work item of the persistent kernel) covers for (D, S, causal).
-int rows_per_cta(int D, int S, bool causal);
+// The forward kernels of this library.
+//   kPersistent  one 128-row query tile per work item, two softmax warpgroups on the two
+//                64-key halves of every score tile (sdpa_fwd_sm100.cu); head dims 64, 128
+//   kPingPong    two 128-row query tiles per work item on one K/V stream, one softmax
+//                warpgroup per tile, separate epilogue warpgroup
+//                (sdpa_fwd_sm100_pingpong.cu); head dims 64, 128
+//   kSharedKv    non-persistent, query tiles of one CTA share every K/V tile
+//                (sdpa_fwd_sm100_shared_kv.cu); head dims 128, 256
+enum KernelKind { kAuto = 0, kPersistent = 1, kPingPong = 2, kSharedKv = 3 };
+
+// The kernel that serves (kernel head dim D, S, causal, B*H): the process-wide forced
+// choice (ta_debug_set_kernel) where it serves D, else the measured default.
+KernelKind select_kernel(int D, int S, bool causal, long long bh);
+void force_kernel(int kind);
+
+// Query rows one work item (CTA) of `kind` covers.
+int rows_per_item(KernelKind kind, int D);
+
+// The ping-pong kernel, reached through launch_sdpa_fwd (grid and scheduler slot set there).
+cudaError_t launch_sdpa_fwd_pingpong(const CUtensorMap& q, const CUtensorMap& k,
+                                     const CUtensorMap& v, const FwdParams& p, int grid, int D,
+                                     bool bf16, bool causal, bool out_f32, cudaStream_t stream);
 
 // The shared-K/V kernel, reached through launch_sdpa_fwd.
 cudaError_t launch_sdpa_fwd_shared_kv(const CUtensorMap& q, const CUtensorMap& k,
@@ -53,11 +73,13 @@ cudaError_t launch_sdpa_fwd_shared_kv(const CUtensorMap& q, const CUtensorMap& k
                                       bool bf16, bool causal, bool out_f32, cudaStream_t stream);
 int rows_per_cta_shared_kv(int D);
 
-// Launches the variant for (D, dtype, causal) on `stream`. Tensor maps are 4-D
-// (D, S, H, B) with a 64 x 128 box and 128-byte swizzle.
-// `o` is a map of the output like q's (used for 16-bit output; ignored when out_f32).
+// Launches the variant of `kind` for (D, dtype, causal) on `stream`. Tensor maps are 4-D
+// (D, S, H, B) with a 64 x 128 box and 128-byte swizzle. `o` is a map of the output like
+// q's (used by the persistent kernel for 16-bit output; ignored otherwise). p.n_qblk must
+// count blocks of rows_per_item(kind, D) rows.
 cudaError_t launch_sdpa_fwd(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
                             const CUtensorMap& o, const FwdParams& p,
-                            int D, bool bf16, bool causal, bool out_f32, cudaStream_t stream);
+                            int D, bool bf16, bool causal, bool out_f32, KernelKind kind,
+                            cudaStream_t stream);
 
 }  // namespace ta
