@@ -140,12 +140,12 @@ struct Layout {
 struct Barriers {
   uint64_t q_full, q_empty;  // Q of the current item loaded / no longer read by QK^T
   uint64_t s_full[3];        // [g % NB]: score tile g complete
-  uint64_t p_full[3];        // [g % NB]: both halves of P_g stored (256 threads)
+  uint64_t p_full[3];        // [g % NB]: both halves of P_g stored (8 softmax warps)
   uint64_t pv_done[4];       // [g % 4]: PV_g (both halves) completed
   uint64_t o_final;          // all PV of the current item completed
-  uint64_t o_empty;          // the epilogue finished reading O (256 threads)
-  uint64_t ep;               // epilogue (m, l) exchange of the two halves (256 threads)
-  uint64_t staged;           // output tile written to the staging buffer (256 threads)
+  uint64_t o_empty;          // the epilogue finished reading O (8 warps)
+  uint64_t ep;               // epilogue (m, l) exchange of the two halves (8 warps)
+  uint64_t staged;           // output tile written to the staging buffer (8 warps)
   uint64_t item_full[2], item_empty[2];
   uint64_t drain;            // both issuers' MMAs completed (2 commits)
   uint64_t never;            // self-test only: a barrier nothing arrives on
@@ -212,13 +212,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&bars->q_empty, 1);
     for (int i = 0; i < NB; ++i) {
       mbar_init(&bars->s_full[i], 1);
-      mbar_init(&bars->p_full[i], 2 * kRowsPerTile);
+      mbar_init(&bars->p_full[i], 8);  // one arrival per softmax warp
     }
     for (int i = 0; i < 4; ++i) mbar_init(&bars->pv_done[i], 1);
     mbar_init(&bars->o_final, 1);
-    mbar_init(&bars->o_empty, 2 * kRowsPerTile);
-    mbar_init(&bars->ep, 2 * kRowsPerTile);
-    mbar_init(&bars->staged, 2 * kRowsPerTile);
+    // Barriers the softmax warps signal take one arrival per warp after a warp sync (256
+    // per-thread arrivals on one barrier are 256 serialised shared-memory atomics).
+    mbar_init(&bars->o_empty, 8);
+    mbar_init(&bars->ep, 8);
+    mbar_init(&bars->staged, 8);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars->item_full[i], 1);
       mbar_init(&bars->item_empty[i], kItemConsumers);
@@ -615,7 +617,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_before();
         if (threadIdx.x % 128 == 0) TRACE(ic, j, 2 + 4 * half);
-        mbar_arrive(&bars->p_full[buf]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->p_full[buf]);
       }
       if (!ok) break;
       // ---- epilogue of the item: merge the two halves. Exchange (m, l) with the partner
@@ -627,7 +630,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       // The thread that issues the output TMA store makes sure the previous item's store has
       // finished reading the staging buffer before anyone passes this exchange.
       if (!OUT_F32 && threadIdx.x == 0) bulk_wait_group_read0();
-      mbar_arrive(&bars->ep);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->ep);
       ok = mbar_wait_bounded(&bars->ep, ic & 1, abort_flag, kTimeoutNs);
       if (ok) ok = mbar_wait_bounded(&bars->o_final, ic & 1, abort_flag, kTimeoutNs);
       ok = __all_sync(0xffffffffu, ok);
@@ -700,12 +704,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // O may now be overwritten by the next item's first P.V.
       tc_fence_before();
-      mbar_arrive(&bars->o_empty);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->o_empty);
       if (!OUT_F32) {
         // Hand the staged tile to the TMA store (issued by thread 0 once all 256 threads
         // wrote their part; rows beyond S are clipped by the tensor map).
         fence_proxy_async_shared();
-        mbar_arrive(&bars->staged);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->staged);
         if (threadIdx.x == 0) {
           if (mbar_wait_bounded(&bars->staged, ic & 1, abort_flag, kTimeoutNs)) {
 #pragma unroll

@@ -212,6 +212,21 @@ __device__ __forceinline__ void pv_mmas(uint32_t d_tmem, uint32_t a_tmem, uint64
   }
 }
 
+// How the MMA issuers wait for P: 0 = suspending try_wait, 1 = polling, 2 = polling with naps.
+#ifndef TA_PP_ISSUER_WAIT
+#define TA_PP_ISSUER_WAIT 0
+#endif
+__device__ __forceinline__ bool issuer_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                            uint64_t timeout_ns) {
+#if TA_PP_ISSUER_WAIT == 1
+  return mbar_wait_spin(bar, parity, abort_flag, timeout_ns);
+#elif TA_PP_ISSUER_WAIT == 2
+  return mbar_wait_spin(bar, parity, abort_flag, timeout_ns, 20);
+#else
+  return mbar_wait_bounded(bar, parity, abort_flag, timeout_ns);
+#endif
+}
+
 __device__ __forceinline__ bool softmax_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                              uint64_t timeout_ns) {
 #if TA_PP_SOFTMAX_WAIT == 1
@@ -485,14 +500,14 @@ __global__ void __launch_bounds__(kThreads, 1)
               ok = mbar_wait_bounded(&bars->o_empty[t], (ic - 1) & 1, abort_flag, kTimeoutNs);
             // P arrives in two halves (keys 0-63, 64-127): P.V of the first half runs while
             // the softmax computes the second. Polling waits: these are on the critical path.
-            if (ok) ok = mbar_wait_spin(&bars->p_half[t], g & 1, abort_flag, kTimeoutNs);
+            if (ok) ok = issuer_wait(&bars->p_half[t], g & 1, abort_flag, kTimeoutNs);
             if (!ok) break;
             TRACE(ic, j, 5 + 4 * t);
             tc_fence_after();
             const uint64_t vd =
                 v_desc + static_cast<uint64_t>(((e_v % L::kKvStages) * L::kTileBytes) >> 4);
             pv_mmas<0, 4>(o_tmem, s_tmem, vd, kIdescPV, j > 0 ? 1u : 0u);
-            ok = mbar_wait_spin(&bars->p_full[t], g & 1, abort_flag, kTimeoutNs);
+            ok = issuer_wait(&bars->p_full[t], g & 1, abort_flag, kTimeoutNs);
             if (!ok) break;
             tc_fence_after();
             pv_mmas<4, 8>(o_tmem, s_tmem, vd, kIdescPV, 1u);
