@@ -47,12 +47,9 @@ inline bool uses_shared_kv(int D, int S, bool causal) {
 // The forward kernels of this library.
 //   kPersistent  one 128-row query tile per work item, two softmax warpgroups on the two
 //                64-key halves of every score tile (sdpa_fwd_sm100.cu); head dims 64, 128
-//   kPingPong    two 128-row query tiles per work item on one K/V stream, one softmax
-//                warpgroup per tile, separate epilogue warpgroup
-//                (sdpa_fwd_sm100_pingpong.cu); head dims 64, 128
 //   kSharedKv    non-persistent, query tiles of one CTA share every K/V tile
 //                (sdpa_fwd_sm100_shared_kv.cu); head dims 128, 256
-enum KernelKind { kAuto = 0, kPersistent = 1, kPingPong = 2, kSharedKv = 3 };
+enum KernelKind { kAuto = 0, kPersistent = 1, kSharedKv = 3 };
 
 // The kernel that serves (kernel head dim D, S, causal, B*H): the process-wide forced
 // choice (ta_debug_set_kernel) where it serves D, else the measured default.
@@ -62,10 +59,6 @@ void force_kernel(int kind);
 // Query rows one work item (CTA) of `kind` covers.
 int rows_per_item(KernelKind kind, int D);
 
-// The ping-pong kernel, reached through launch_sdpa_fwd (grid and scheduler slot set there).
-cudaError_t launch_sdpa_fwd_pingpong(const CUtensorMap& q, const CUtensorMap& k,
-                                     const CUtensorMap& v, const FwdParams& p, int grid, int D,
-                                     bool bf16, bool causal, bool out_f32, cudaStream_t stream);
 
 // The shared-K/V kernel, reached through launch_sdpa_fwd.
 cudaError_t launch_sdpa_fwd_shared_kv(const CUtensorMap& q, const CUtensorMap& k,

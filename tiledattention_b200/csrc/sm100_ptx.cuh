@@ -82,40 +82,6 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
 }
 
-// Non-blocking test of the phase with the given parity.
-__device__ __forceinline__ bool mbar_test_wait(uint32_t bar_addr, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar_addr), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Like mbar_wait_bounded, but polls without letting the hardware suspend the thread: for a
-// thread on the critical path that expects the phase soon (a suspended try_wait was measured
-// to resume ~300 clocks after the phase completed). Same limits: abort flag, timeout_ns.
-// sleep_ns > 0 naps that long between polls (frees issue slots for warps that share the SM
-// sub-partition).
-__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity,
-                                               volatile int* abort_flag, uint64_t timeout_ns,
-                                               unsigned sleep_ns = 0) {
-  const uint32_t a = smem_u32(bar);
-  if (mbar_test_wait(a, parity)) return true;
-  const uint64_t t0 = global_timer_ns();
-  for (uint32_t it = 1;; ++it) {
-    if (sleep_ns) __nanosleep(sleep_ns);
-    if (mbar_test_wait(a, parity)) return true;
-    if ((it & 255u) == 0u) {
-      if (*abort_flag) return false;
-      if (global_timer_ns() - t0 > timeout_ns) return false;
-    }
-  }
-}
-
 // ------------------------------------------------------------------ TMA
 // 4-D tiled bulk tensor load global -> shared, completion signalled on `bar`
 // through complete_tx. No multicast.
@@ -153,17 +119,6 @@ __device__ __forceinline__ void bulk_wait_group0() {
 // Makes this thread's generic-proxy shared-memory writes visible to the async proxy (TMA).
 __device__ __forceinline__ void fence_proxy_async_shared() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
-// Prefetch a 4-D tile into L2 only (no shared memory, no completion tracking): a later
-// tma_load_4d of the same tile then reads from L2 instead of HBM.
-__device__ __forceinline__ void tma_prefetch_l2_4d(const CUtensorMap* map, int c0, int c1, int c2,
-                                                   int c3) {
-  asm volatile(
-      "cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
-          reinterpret_cast<uint64_t>(map)),
-      "r"(c0), "r"(c1), "r"(c2), "r"(c3)
-      : "memory");
 }
 
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
@@ -211,47 +166,6 @@ __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// The same two MMAs with the descriptor offsets (16-byte units) and the accumulate flag as
-// immediates: the adds happen inside the asm block, so an unrolled sequence keeps only the
-// base descriptors in registers (a thread issuing MMAs on few registers needs that).
-template <uint32_t kAOff, uint32_t kBOff, uint32_t kAcc>
-__device__ __forceinline__ void mma_ss_imm(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                           uint32_t idesc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t.reg .b64 a, b;\n\t"
-      "add.s64 a, %1, %4;\n\t"
-      "add.s64 b, %2, %5;\n\t"
-      "setp.ne.b32 p, %6, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "n"(kAOff), "n"(kBOff), "n"(kAcc)
-      : "memory");
-}
-template <uint32_t kATmemOff, uint32_t kBOff, uint32_t kAcc>
-__device__ __forceinline__ void mma_ts_imm(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
-                                           uint32_t idesc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t.reg .b64 b;\n\t.reg .b32 a;\n\t"
-      "add.u32 a, %1, %4;\n\t"
-      "add.s64 b, %2, %5;\n\t"
-      "setp.ne.b32 p, %6, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "n"(kATmemOff), "n"(kBOff), "n"(kAcc)
-      : "memory");
-}
-// Same as mma_ts_imm with the accumulate flag given at run time.
-template <uint32_t kATmemOff, uint32_t kBOff>
-__device__ __forceinline__ void mma_ts_imm_acc(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
-                                               uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t.reg .b64 b;\n\t.reg .b32 a;\n\t"
-      "add.u32 a, %1, %5;\n\t"
-      "add.s64 b, %2, %6;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(acc), "n"(kATmemOff), "n"(kBOff)
       : "memory");
 }
 
@@ -319,17 +233,6 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
       "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
       "r"(r[29]), "r"(r[30]), "r"(r[31])
-      : "memory");
-}
-
-// Each thread of the warp writes 16 consecutive 32-bit columns of its own TMEM lane.
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
-      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
-      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
-      "r"(r[15])
       : "memory");
 }
 
