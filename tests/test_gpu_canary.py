@@ -28,7 +28,7 @@ def _inputs(B, H, S, D, dtype, seed):
     (1, 2, 300, 96, False),     # persistent kernel on the 128 tile, columns 96-127 not written
     (1, 2, 257, 64, True),
     (1, 2, 300, 200, True),     # shared-K/V kernel on the 256 tile
-    (1, 1, 16384, 128, False),  # shared-K/V kernel at D=128
+    (1, 16, 32768, 128, False), # shared-K/V kernel at D=128 (B*H*S^2 = 2^34)
 ])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_output_window_only(B, H, S, D, causal, dtype):

@@ -201,8 +201,8 @@ def test_head_dim_256(S, causal, dtype):
 
 def test_long_rows_shared_kv_kernel():
     """Long head-dim-128 rows run on the shared-K/V (two query tiles per CTA) kernel:
-    non-causal from S = 16384, causal from S = 65536."""
-    q, k, v = _inputs(1, 1, 16384, 128, torch.bfloat16, 31)
+    non-causal once B*H*S^2 >= 2^34 (here B*H 16, S 32768), causal from S = 65536."""
+    q, k, v = _inputs(1, 16, 32768, 128, torch.bfloat16, 31)
     _check(q, k, v, False, oracle_rows=(0, 64))
     q, k, v = _inputs(1, 1, 65536, 128, torch.bfloat16, 32)
     _check(q, k, v, True, oracle_rows=(65536 - 32, 65536))
@@ -317,10 +317,18 @@ def test_head_dim_64_long_rows_fp16():
 
 
 def test_unpadded_head_dim_on_shared_kv_kernel():
-    """Head dim 96 over a non-causal S=16384 runs on the shared-K/V kernel at kernel head dim
-    128 with predicated output stores (no padded copies)."""
-    q, k, v = _inputs(1, 1, 16384, 96, torch.bfloat16, 97)
-    _check(q, k, v, False, oracle_rows=(0, 64))
+    """Head dim 96 over a non-causal S=16384 on the shared-K/V kernel (forced: the dispatch
+    sends one head of this length to the persistent kernel) at kernel head dim 128 with
+    predicated output stores (no padded copies)."""
+    from tiledattention_b200 import _native
+
+    lib = _native.load_library()
+    lib.ta_debug_set_kernel(3)
+    try:
+        q, k, v = _inputs(1, 1, 16384, 96, torch.bfloat16, 97)
+        _check(q, k, v, False, oracle_rows=(0, 64))
+    finally:
+        lib.ta_debug_set_kernel(0)
 
 
 def test_config3_full_shape_every_pair():

@@ -851,11 +851,10 @@ void force_kernel(int kind) {
 }
 
 KernelKind select_kernel(int D, int S, bool causal, long long bh) {
-  (void)bh;
   const int forced = g_forced_kernel.load(std::memory_order_relaxed);
   if (forced == kSharedKv && (D == 128 || D == 256)) return kSharedKv;
   if (forced == kPersistent && (D == 64 || D == 128)) return kPersistent;
-  if (uses_shared_kv(D, S, causal)) return kSharedKv;
+  if (uses_shared_kv(D, S, causal, bh)) return kSharedKv;
   return kPersistent;
 }
 

@@ -26,22 +26,20 @@ struct FwdParams {
                            // kernel writes only these columns
 };
 
-// Whether (D, S, causal) runs on the shared-K/V kernel (sdpa_fwd_sm100_shared_kv.cu): head
-// dim 256 always; head dim 128 from kSharedKvMinSeq keys on (causal) or
-// kSharedKvMinSeqNonCausal (non-causal), where the persistent one-tile kernel's lower
-// start-up cost no longer outweighs loading each K/V tile once per 128 query rows instead of
-// once per 256 (crossovers measured on B200).
-#ifndef TA_SKV_MIN_SEQ
-#define TA_SKV_MIN_SEQ 65536
-#endif
-#ifndef TA_SKV_MIN_SEQ_NONCAUSAL
-#define TA_SKV_MIN_SEQ_NONCAUSAL 16384
-#endif
-constexpr int kSharedKvMinSeq = TA_SKV_MIN_SEQ;
-constexpr int kSharedKvMinSeqNonCausal = TA_SKV_MIN_SEQ_NONCAUSAL;
-inline bool uses_shared_kv(int D, int S, bool causal) {
-  return D == 256 ||
-         (D == 128 && S >= (causal ? kSharedKvMinSeq : kSharedKvMinSeqNonCausal));
+// Whether (D, S, causal, B*H) runs on the shared-K/V kernel (sdpa_fwd_sm100_shared_kv.cu):
+// head dim 256 always; head dim 128 where loading each K/V tile once per 256 query rows
+// instead of once per 128 outweighs the persistent one-tile kernel's scheduling and lower
+// start-up cost. Crossovers measured on B200 over B*H in {8, 16, 64, 256} and S from 4096 to
+// 65536 (both kernels within 3 % of each other near the lines):
+//   non-causal  B*H * S^2 >= 2^34 (S 8192 from B*H 256, 16384 from 64, 32768 from 16,
+//               65536 from 4);
+//   causal      S >= 65536, or S >= 32768 with B*H >= 256.
+inline bool uses_shared_kv(int D, int S, bool causal, long long bh) {
+  if (D == 256) return true;
+  if (D != 128) return false;
+  const double s = static_cast<double>(S);
+  if (!causal) return static_cast<double>(bh) * s * s >= 17179869184.0;  // 2^34
+  return S >= 65536 || (S >= 32768 && bh >= 256);
 }
 
 // The forward kernels of this library.
