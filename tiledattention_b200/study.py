@@ -10,8 +10,10 @@ benchmark-gb10/results/benchmark_results.csv:1, so results line up with its GB10
     method, baseline_name, dtype, causal, B, H, S, D, flops_forward, median_ms, p95_ms,
     throughput_tokens_per_s, tflops_per_s, approx_bw_gbps, status, status_detail
 
-Methods: ``tiledattention`` (this package) and the torch baselines ``torch_sdpa`` (auto
-backend) and ``torch_sdpa_math`` (math backend, on the GPU). Timing follows the
+Methods: ``tiledattention`` (this package, automatic kernel choice),
+``tiledattention_persistent`` / ``tiledattention_shared_kv`` (one forward kernel forced, for
+dispatch sweeps; --batch/--heads widen the sweep beyond B=1, H=8) and the torch baselines
+``torch_sdpa`` (auto backend) and ``torch_sdpa_math`` (math backend, on the GPU). Timing follows the
 reference's time_cuda_callable (run_study.py:48-75): warm-up, then a CUDA-event pair around
 every call, median and p95; the metric formulas are run_study.py:78-148. Failures are
 recorded as rows with status "error" (run_study.py:338-395) instead of aborting the sweep.
@@ -92,6 +94,17 @@ def run_sweep(seqs, dims, dtypes, causals, methods, warmup=5, iters=15, b=1, h=8
     from torch.nn.attention import SDPBackend, sdpa_kernel
 
     import tiledattention_b200 as ta
+    from tiledattention_b200 import _native
+
+    def forced(kind):
+        def run(q, k, v, c):
+            lib = _native.load_library()
+            lib.ta_debug_set_kernel(kind)
+            try:
+                return ta.sdpa(q, k, v, causal=c)
+            finally:
+                lib.ta_debug_set_kernel(0)
+        return run
 
     def torch_math(q, k, v, causal):
         with sdpa_kernel(SDPBackend.MATH):
@@ -99,6 +112,8 @@ def run_sweep(seqs, dims, dtypes, causals, methods, warmup=5, iters=15, b=1, h=8
 
     impls = {
         "tiledattention": lambda q, k, v, c: ta.sdpa(q, k, v, causal=c),
+        "tiledattention_persistent": forced(1),
+        "tiledattention_shared_kv": forced(3),
         "torch_sdpa": lambda q, k, v, c: torch.nn.functional.scaled_dot_product_attention(
             q, k, v, is_causal=c),
         "torch_sdpa_math": torch_math,
@@ -142,9 +157,14 @@ def main(argv=None) -> None:
     ap.add_argument("--methods", nargs="+", default=["tiledattention", "torch_sdpa", "torch_sdpa_math"])
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--iters", type=int, default=15)
+    ap.add_argument("--batch", type=int, nargs="+", default=[1])
+    ap.add_argument("--heads", type=int, nargs="+", default=[8])
     args = ap.parse_args(argv)
-    rows = run_sweep(args.seq, args.dims, args.dtypes, [c == "True" for c in args.causal],
-                     args.methods, args.warmup, args.iters)
+    rows = []
+    for b in args.batch:
+        for h in args.heads:
+            rows += run_sweep(args.seq, args.dims, args.dtypes, [c == "True" for c in args.causal],
+                              args.methods, args.warmup, args.iters, b=b, h=h)
     write_csv(rows, args.out)
     print(f"wrote {len(rows)} rows to {args.out}")
 
