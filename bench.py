@@ -170,8 +170,8 @@ class ClockSampler:
             "samples": len(self.samples),
         }
 
-    def util_median(self):
-        return statistics.median(self.util) if self.util else None
+    def util_max(self):
+        return max(self.util) if self.util else None
 
 
 def make_inputs(torch, pairs, S, D, dtype, pair_start, device=None, pinned=False):
@@ -412,6 +412,11 @@ def main():
         torch.cuda.synchronize(device)
         return [s_.elapsed_time(e_) for s_, e_ in zip(starts, ends)], out
 
+    # The process group's first collectives set up NCCL communicators (tens of ms); run them
+    # here so that no timed step waits for that set-up.
+    barrier()
+    max_over_ranks(0.0)
+    torch.cuda.synchronize(device)
     sampler = ClockSampler(torch, device)
     for _ in range(args.warmup):
         flush.zero_()
@@ -442,14 +447,10 @@ def main():
         mine = {"rank": rank, "pairs": pairs,
                 "step_ms_median": round(statistics.median(step_ms), 4),
                 "step_ms_min": round(min(step_ms), 4), "step_ms_max": round(max(step_ms), 4),
-                "sm_mhz": clocks["sm_mhz"], "gpu_util_median": sampler.util_median(),
-                "reasons": clocks["reasons"]}
-        gathered = [None] * world
-        dist.all_gather_object(gathered, mine)
-        ranks = {"per_rank": gathered,
-                 "gpus_busy": sum(1 for r in gathered if (r["gpu_util_median"] or 0) > 0),
-                 "step_ms_spread": round(max(r["step_ms_median"] for r in gathered) -
-                                         min(r["step_ms_median"] for r in gathered), 4)}
+                "step_max_index": int(max(range(len(step_ms)), key=lambda i: step_ms[i])),
+                "kernel_ms_total": round(sum(step_ms), 4),
+                "sm_mhz": clocks["sm_mhz"], "reasons": clocks["reasons"]}
+        ranks = {"mine": mine}
 
     # ---- sustained regime: several seconds of the same step, with its own clock record
     sustained = None
@@ -463,9 +464,22 @@ def main():
         sus_clocks = sus_sampler.stop()
         del o
         sus_total = max_over_ranks(sum(sus_ms))
+        sus_util = sus_sampler.util_max()
         sus_value = job_flops * n_sus / (sus_total / 1e3) / 1e12
         sustained = {"value": round(sus_value, 2), "steps": n_sus,
                      "seconds": round(sus_total / 1e3, 2), "clocks": sus_clocks}
+        if ranks is not None:
+            ranks["mine"]["gpu_util_max"] = sus_util
+
+    # ---- per-rank record gathered on rank 0 (after the sustained loop, whose seconds of work
+    # give NVML's utilisation counter, averaged over its own window, time to see each GPU busy)
+    if ranks is not None:
+        gathered = [None] * world
+        dist.all_gather_object(gathered, ranks["mine"])
+        ranks = {"per_rank": gathered,
+                 "gpus_busy": sum(1 for r in gathered if (r.get("gpu_util_max") or 0) > 0),
+                 "step_ms_spread": round(max(r["step_ms_median"] for r in gathered) -
+                                         min(r["step_ms_median"] for r in gathered), 4)}
 
     # ---- same-box context: torch's own GPU SDPA on the same inputs, timed the same way
     context = None
