@@ -400,10 +400,15 @@ def main():
         return float(t.item())
 
     def timed_loop(n, fn):
-        """n steps, each after an (untimed) L2 flush; per-step device times in ms."""
+        """n steps, each after an (untimed) L2 flush; per-step device times in ms. A ~50 ms
+        device-side sleep is enqueued first (outside every timed window) so that the host has
+        enqueued the steps before the GPU reaches them: otherwise a host-side hiccup while the
+        first steps are enqueued leaves the GPU idle between a step's start event and its kernel
+        (seen as one 2 ms step of 0.14 ms ones at N=8)."""
         starts = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
         ends = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
         out = None
+        torch.cuda._sleep(int(50e-3 * 2.0e9))  # ~50 ms at up to 2 GHz
         for i in range(n):
             flush.zero_()  # L2 flush, enqueued before the start event: not timed
             starts[i].record(stream)
