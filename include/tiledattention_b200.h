@@ -204,8 +204,8 @@ void ta_debug_set_selftest(int stall, unsigned long long timeout_ns);
 
 /*
  * ta_debug_set_kernel — process-wide choice of the forward kernel, for tests and A/B timing:
- * 0 = automatic (default), 1 = persistent split-halves kernel (head dims 64/128), 2 = deep-
- * buffered kernel (64/128), 3 = shared-K/V kernel (128/256); other values mean automatic. A choice that does not serve a call's kernel
+ * 0 = automatic (default), 1 = persistent split-halves kernel (head dims 64/128), 3 =
+ * shared-K/V kernel (128/256); other values mean automatic. A choice that does not serve a call's kernel
  * head dim is ignored for that call. Results agree within the parity
  * tolerance whichever kernel runs. No reference counterpart.
  */

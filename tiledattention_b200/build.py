@@ -22,7 +22,7 @@ REPO_DIR = os.path.dirname(PKG_DIR)
 CSRC = os.path.join(PKG_DIR, "csrc")
 OUT_DIR = os.path.join(PKG_DIR, "_lib")
 OUT = os.path.join(OUT_DIR, "libtiledattention_b200.so")
-SOURCES = ["capi.cu", "sdpa_fwd_sm100.cu", "sdpa_fwd_sm100_shared_kv.cu", "sdpa_fwd_sm100_deep.cu", "lse_combine.cu", "noalloc_split.cu", "peer_merge.cu"]
+SOURCES = ["capi.cu", "sdpa_fwd_sm100.cu", "sdpa_fwd_sm100_shared_kv.cu", "lse_combine.cu", "noalloc_split.cu", "peer_merge.cu"]
 HEADERS = ["sm100_ptx.cuh", "sdpa_common.cuh", "sdpa_fwd_sm100.h", "lse_combine.h", "capi_internal.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 # One-call host launcher (CPython extension over libtorch; no device code): see

@@ -211,7 +211,7 @@ int run_forward(const void* q, const void* k, const void* v, void* o, bool out_f
       ta::select_kernel(kd, S, causal != 0, static_cast<long long>(B) * H);
   CUtensorMap mo;
   memset(&mo, 0, sizeof(mo));
-  if (!out_f32 && (kind == ta::kPersistent || kind == ta::kDeep) &&
+  if (!out_f32 && kind == ta::kPersistent &&
       (rc = make_map(&mo, o, B, H, S, D, o_strides, dtype, "o")))
     return rc;
 

@@ -824,8 +824,6 @@ cudaError_t launch_sdpa_fwd(const CUtensorMap& q, const CUtensorMap& k, const CU
   const unsigned int slot = g_sched_next[dev].fetch_add(1, std::memory_order_relaxed) % kSchedSlots;
   p.sched = g_sched_base[dev].load(std::memory_order_relaxed) + 2 * slot;
   const int grid = static_cast<int>(items < sms ? items : sms);
-  if (kind == kDeep)
-    return launch_sdpa_fwd_deep(q, k, v, o, p, grid, D, bf16, causal, out_f32, stream);
 #define TA_DISPATCH(DD, BB, CC, FF)                                               \
   if (D == DD && bf16 == BB && causal == CC && out_f32 == FF)                     \
     return launch_variant<DD, BB, CC, FF>(q, k, v, o, p, grid, stream);
@@ -848,15 +846,14 @@ std::atomic<int> g_forced_kernel{kAuto};
 }  // namespace
 
 void force_kernel(int kind) {
-  g_forced_kernel.store(kind == kPersistent || kind == kDeep || kind == kSharedKv ? kind : kAuto,
+  g_forced_kernel.store(kind == kPersistent || kind == kSharedKv ? kind : kAuto,
                         std::memory_order_relaxed);
 }
 
 KernelKind select_kernel(int D, int S, bool causal, long long bh) {
   const int forced = g_forced_kernel.load(std::memory_order_relaxed);
   if (forced == kSharedKv && (D == 128 || D == 256)) return kSharedKv;
-  if ((forced == kPersistent || forced == kDeep) && (D == 64 || D == 128))
-    return static_cast<KernelKind>(forced);
+  if (forced == kPersistent && (D == 64 || D == 128)) return kPersistent;
   if (uses_shared_kv(D, S, causal, bh)) return kSharedKv;
   return kPersistent;
 }

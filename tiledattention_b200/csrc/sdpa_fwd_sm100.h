@@ -45,11 +45,9 @@ inline bool uses_shared_kv(int D, int S, bool causal, long long bh) {
 // The forward kernels of this library.
 //   kPersistent  one 128-row query tile per work item, two softmax warpgroups on the two
 //                64-key halves of every score tile (sdpa_fwd_sm100.cu); head dims 64, 128
-//   kDeep        persistent, one softmax warpgroup owning whole rows, one accumulator and
-//                three score buffers (sdpa_fwd_sm100_deep.cu); head dims 64, 128
 //   kSharedKv    non-persistent, query tiles of one CTA share every K/V tile
 //                (sdpa_fwd_sm100_shared_kv.cu); head dims 128, 256
-enum KernelKind { kAuto = 0, kPersistent = 1, kDeep = 2, kSharedKv = 3 };
+enum KernelKind { kAuto = 0, kPersistent = 1, kSharedKv = 3 };
 
 // The kernel that serves (kernel head dim D, S, causal, B*H): the process-wide forced
 // choice (ta_debug_set_kernel) where it serves D, else the measured default.
@@ -65,11 +63,6 @@ cudaError_t launch_sdpa_fwd_shared_kv(const CUtensorMap& q, const CUtensorMap& k
                                       const CUtensorMap& v, const FwdParams& p, int D,
                                       bool bf16, bool causal, bool out_f32, cudaStream_t stream);
 int rows_per_cta_shared_kv(int D);
-
-// The deep-buffered kernel, reached through launch_sdpa_fwd (grid and scheduler slot set there).
-cudaError_t launch_sdpa_fwd_deep(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
-                                 const CUtensorMap& o, const FwdParams& p, int grid, int D,
-                                 bool bf16, bool causal, bool out_f32, cudaStream_t stream);
 
 // Launches the variant of `kind` for (D, dtype, causal) on `stream`. Tensor maps are 4-D
 // (D, S, H, B) with a 64 x 128 box and 128-byte swizzle. `o` is a map of the output like
