@@ -73,12 +73,17 @@ def make_row(method: str, dtype_name: str, causal: bool, b: int, h: int, s: int,
     return row
 
 
-def time_cuda_callable(torch, fn, warmup: int, iters: int) -> tuple[float, float]:
+def time_cuda_callable(torch, fn, warmup: int, iters: int, flush=None) -> tuple[float, float]:
+    """Median and p95 of CUDA-event times of fn (run_study.py:48-75). `flush`: a device
+    buffer larger than L2 that is rewritten before every timed call, outside the events, so
+    every call starts from a cold L2 (an option beyond the reference's timing)."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
     timings = []
     for _ in range(iters):
+        if flush is not None:
+            flush.zero_()
         start = torch.cuda.Event(enable_timing=True)
         end = torch.cuda.Event(enable_timing=True)
         start.record()
@@ -89,7 +94,8 @@ def time_cuda_callable(torch, fn, warmup: int, iters: int) -> tuple[float, float
     return statistics.median(timings), p95(timings)
 
 
-def run_sweep(seqs, dims, dtypes, causals, methods, warmup=5, iters=15, b=1, h=8, seed=1234):
+def run_sweep(seqs, dims, dtypes, causals, methods, warmup=5, iters=15, b=1, h=8, seed=1234,
+              flush_l2=False):
     import torch
     from torch.nn.attention import SDPBackend, sdpa_kernel
 
@@ -120,6 +126,7 @@ def run_sweep(seqs, dims, dtypes, causals, methods, warmup=5, iters=15, b=1, h=8
     }
     rows = []
     dev = torch.device("cuda")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev) if flush_l2 else None
     for causal in causals:
         for dtype_name in dtypes:
             dtype = getattr(torch, dtype_name)
@@ -131,7 +138,7 @@ def run_sweep(seqs, dims, dtypes, causals, methods, warmup=5, iters=15, b=1, h=8
                         fn = impls[method]
                         try:
                             med, tail = time_cuda_callable(torch, lambda: fn(q, k, v, causal),
-                                                           warmup, iters)
+                                                           warmup, iters, flush)
                             rows.append(make_row(method, dtype_name, causal, b, h, s, d, med, tail))
                         except Exception as exc:  # recorded, like run_study.py:338-395
                             rows.append(make_row(method, dtype_name, causal, b, h, s, d, None,
@@ -159,12 +166,15 @@ def main(argv=None) -> None:
     ap.add_argument("--iters", type=int, default=15)
     ap.add_argument("--batch", type=int, nargs="+", default=[1])
     ap.add_argument("--heads", type=int, nargs="+", default=[8])
+    ap.add_argument("--flush-l2", action="store_true",
+                    help="rewrite a 256 MB buffer before every timed call (cold L2)")
     args = ap.parse_args(argv)
     rows = []
     for b in args.batch:
         for h in args.heads:
             rows += run_sweep(args.seq, args.dims, args.dtypes, [c == "True" for c in args.causal],
-                              args.methods, args.warmup, args.iters, b=b, h=h)
+                              args.methods, args.warmup, args.iters, b=b, h=h,
+                              flush_l2=args.flush_l2)
     write_csv(rows, args.out)
     print(f"wrote {len(rows)} rows to {args.out}")
 
