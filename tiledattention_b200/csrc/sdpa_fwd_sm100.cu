@@ -106,8 +106,8 @@ constexpr int kNoItem = -1;  // Item::split of "no item left"
 // (0: never). Worth it only where the MUFU is the limit and the MMA work is small (D=64).
 template <int D>
 __host__ __device__ constexpr int poly_every() {
-#ifdef TA_POLY_EVERY_D64
-  return D == 64 ? TA_POLY_EVERY_D64 : 0;
+#if defined(TA_POLY_EVERY_D64) && defined(TA_POLY_EVERY_D128)
+  return D == 64 ? TA_POLY_EVERY_D64 : TA_POLY_EVERY_D128;
 #else
   return D == 64 ? 4 : 0;
 #endif
