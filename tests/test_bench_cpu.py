@@ -22,6 +22,10 @@ def test_reference_arm_json_line():
     assert d["impl"] == "reference" and d["metric"] == "sdpa_fwd_tflops"
     assert d["unit"] == "TFLOP/s" and d["higher_is_better"] is True and d["steps"] == 1
     assert d["config"]["workload"] == "llama_prefill_b8_h32_s4096_d128_bf16_causal"
+    # the GPU arm's config describes the same workload with the same keys and values
+    import bench
+
+    assert d["config"] == bench.workload_config(bench.WORKLOAD)
     assert d["value"] > 0 and d["cpu_baseline"]["value"] == d["value"]
     assert d["cpu_baseline"]["kind"] in ("port", "reference") and d["cpu_baseline"]["cores"] >= 1
     assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0,
