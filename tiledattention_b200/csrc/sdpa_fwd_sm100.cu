@@ -25,19 +25,21 @@
 //
 // Work: one item = one (key slice, batch*head pair, 128-row query block). The grid has at
 // most one CTA per SM; each CTA takes items from a global counter until they run out, in
-// groups of (b,h) pairs whose K/V fit in L2, longest causal blocks of a group first. Consecutive items of a CTA
-// overlap: while the softmax warps write the output of item i, the producer has loaded
-// Q and the first K tiles of item i+1 and the QK^T issuer has computed its first scores.
+// groups of (b,h) pairs whose K/V fit in L2, longest causal blocks of a group first.
+// Consecutive items of a CTA overlap: while the epilogue warps write the output of item i,
+// the softmax warps already work on item i+1, whose Q and first K tiles the producer loaded
+// and whose first scores the QK^T issuer computed during item i's last tiles.
 //
-// CTA organisation (one CTA per SM: all 512 TMEM columns):
-//   warps 0-3  softmax of key columns 0-63 of every score tile (half a), accumulator O_a
-//   warps 4-7  softmax of key columns 64-127 (half b), accumulator O_b; in both, thread
-//              lane i of warp w owns query row 32*(w%4) + i of the item (its TMEM lane);
-//              then the epilogue of the item
-//   warp  8    scheduler + TMA producer: per item Q, then K_0 .. K_{NB-1}, V_j, K_{j+NB}
-//   warp  9    TMEM allocator and P.V issuer (one elected thread)
-//   warp 10    QK^T issuer (one elected thread)
-//   warp 11    idle (completes the third warpgroup for the register split)
+// CTA organisation (512 threads, one CTA per SM: all 512 TMEM columns):
+//   warps 0-3   softmax of key columns 0-63 of every score tile (half a), accumulator O_a
+//   warps 4-7   softmax of key columns 64-127 (half b), accumulator O_b; in both, thread
+//               lane i of warp w owns query row 32*(w%4) + i of the item (its TMEM lane);
+//               at the end of an item each half hands its (m, l) to the epilogue
+//   warp  8     scheduler + TMA producer: per item Q, then K_0 .. K_{NB-1}, V_j, K_{j+NB}
+//   warp  9     TMEM allocator and P.V issuer (one elected thread)
+//   warp 10     QK^T issuer (one elected thread)
+//   warp 11     idle (completes the third warpgroup for the register split)
+//   warps 12-15 epilogue: merges O_a and O_b, normalises, stages the tile for one TMA store
 // Tensor memory: NB score buffers of 128 columns (NB = 3 at D=64, 2 at D=128), then
 // O_a and O_b (D columns each). The g-th score tile a CTA processes (counted over all its
 // items) lives in buffer g%NB; each half's P (16-bit, two per column) overwrites the first
@@ -75,31 +77,36 @@ using common::report;
 constexpr int kRowsPerTile = 128;  // query rows per item (= TMEM lanes)
 constexpr int kKeysPerTile = 128;  // keys per K/V tile
 constexpr int kKeysPerHalf = 64;   // keys of one half (one softmax warpgroup)
-constexpr int kThreads = 384;
-// Register split: the kernel is built for kLaunchRegs per thread (launch bounds 384 x 1);
-// after start-up the producer/MMA warpgroup gives registers back (setmaxnreg.dec to
-// kSideRegs) and the two softmax warpgroups take them (setmaxnreg.inc to kSoftmaxRegs).
-// 2*128*kSoftmaxRegs + 128*kSideRegs == 384*kLaunchRegs, so the increase always fits
-// in the block's launch allocation; the host refuses to launch a build whose register
-// count differs from kLaunchRegs.
-constexpr int kLaunchRegs = 168;
+constexpr int kThreads = 512;
+// Register split: the kernel is built for kLaunchRegs per thread (launch bounds 512 x 1);
+// after start-up the producer/MMA warpgroup and the epilogue warpgroup give registers back
+// (setmaxnreg.dec to kSideRegs / kEpilogueRegs) and the two softmax warpgroups take them
+// (setmaxnreg.inc to kSoftmaxRegs). The sum equals the launch allocation, so the increase
+// always fits; the host refuses to launch a build whose register count differs from
+// kLaunchRegs.
+constexpr int kLaunchRegs = 128;
 #ifndef TA_SOFTMAX_REGS
-#define TA_SOFTMAX_REGS 192
-#define TA_SIDE_REGS 120
+#define TA_SOFTMAX_REGS 184
+#define TA_EPILOGUE_REGS 72
+#define TA_SIDE_REGS 72
 #endif
 constexpr int kSoftmaxRegs = TA_SOFTMAX_REGS;
+constexpr int kEpilogueRegs = TA_EPILOGUE_REGS;
 constexpr int kSideRegs = TA_SIDE_REGS;
-static_assert(2 * 128 * kSoftmaxRegs + 128 * kSideRegs == kThreads * kLaunchRegs,
+static_assert(2 * 128 * kSoftmaxRegs + 128 * kEpilogueRegs + 128 * kSideRegs ==
+                  kThreads * kLaunchRegs,
               "register split must match the launch allocation");
 constexpr int kProducerWarp = 8;
 constexpr int kPvWarp = 9;
 constexpr int kQkWarp = 10;
+constexpr int kEpilogueWarp0 = 12;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;      // log2 units
 constexpr int kSumChains = 4;  // independent row-sum accumulators (short dependency chains)
 constexpr uint64_t kDefaultTimeoutNs = 1000000000ull;  // 1 s per wait
-// Item-broadcast consumers: the two issuer threads and lane 0 of each softmax warp.
-constexpr int kItemConsumers = 2 + 8;
+// Item-broadcast consumers: the two issuer threads and lane 0 of each softmax and epilogue
+// warp.
+constexpr int kItemConsumers = 2 + 8 + 4;
 constexpr int kNoItem = -1;  // Item::split of "no item left"
 
 // Every kPolyEvery-th element pair computes exp2 on the FMA pipe instead of the MUFU
@@ -143,9 +150,11 @@ struct Barriers {
   uint64_t p_full[3];        // [g % NB]: both halves of P_g stored (8 softmax warps)
   uint64_t pv_done[4];       // [g % 4]: PV_g (both halves) completed
   uint64_t o_final;          // all PV of the current item completed
-  uint64_t o_empty;          // the epilogue finished reading O (8 warps)
-  uint64_t ep;               // epilogue (m, l) exchange of the two halves (8 warps)
-  uint64_t staged;           // output tile written to the staging buffer (8 warps)
+  uint64_t o_empty;          // the epilogue finished reading O_a, O_b (4 epilogue warps)
+  uint64_t ml_full[2];       // [item % 2]: both halves' (m, l) of the item written (8 warps)
+  uint64_t ml_empty[2];      // [item % 2]: the epilogue read them (4 warps)
+  uint64_t stage_free;       // the previous output tile's TMA store read the staging buffer
+  uint64_t staged;           // output tile written to the staging buffer (4 warps)
   uint64_t item_full[2], item_empty[2];
   uint64_t drain;            // both issuers' MMAs completed (2 commits)
   uint64_t never;            // self-test only: a barrier nothing arrives on
@@ -185,6 +194,34 @@ __device__ __forceinline__ void trace_item(const FwdParams& p, int ic, int ev) {
 // OUT_F32: write o as fp32 (the normalised partial output of one key slice) instead of
 // the input dtype. Items: n_split x B*H x n_qblk; slice s covers keys
 // [kv_begin + s*split_len, min(kv_end, kv_begin + (s+1)*split_len)).
+// S = Q K^T for one 128x128 score tile: D/16 MMAs of K=16. Q and K tiles are K-major,
+// 128-byte swizzled, in chunks of 64 columns (16 KB per chunk of 128 rows); step kk reads
+// columns 16kk..16kk+15: chunk kk/4, 32 bytes into the swizzle atom per kk%4.
+template <int D, int kk = 0>
+__device__ __forceinline__ void qk_mmas(uint32_t d_tmem, uint64_t qd, uint64_t kd, uint32_t idesc) {
+  if constexpr (kk < D / 16) {
+    constexpr uint32_t off = ((kk >> 2) * (kRowsPerTile * 128) + (kk & 3) * 32) >> 4;
+    mma_ss_imm<off, off, (kk > 0 ? 1u : 0u)>(d_tmem, qd, kd, idesc);
+    qk_mmas<D, kk + 1>(d_tmem, qd, kd, idesc);
+  }
+}
+
+// O_hh (+)= P_hh V_hh: the 64 keys of half hh in 4 MMAs of K=16. P comes from tensor memory
+// (16-bit pairs, 8 columns per 16 keys); V is MN-major, 128-byte swizzled (16 key rows =
+// 2 KB). `acc` is the accumulate flag of the half's first MMA.
+template <int HH, int k4 = 0>
+__device__ __forceinline__ void pv_half_mmas(uint32_t d_tmem, uint32_t a_tmem, uint64_t vd,
+                                             uint32_t idesc, uint32_t acc) {
+  if constexpr (k4 < kKeysPerHalf / 16) {
+    constexpr uint32_t off = ((HH * (kKeysPerHalf / 16) + k4) * 16 * 128) >> 4;
+    if constexpr (k4 == 0)
+      mma_ts_imm_acc<0, off>(d_tmem, a_tmem, vd, idesc, acc);
+    else
+      mma_ts_imm<k4 * 8, off, 1u>(d_tmem, a_tmem, vd, idesc);
+    pv_half_mmas<HH, k4 + 1>(d_tmem, a_tmem, vd, idesc, acc);
+  }
+}
+
 template <int D, bool BF16, bool CAUSAL, bool OUT_F32>
 __global__ void __launch_bounds__(kThreads, 1)
     sdpa_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q,
@@ -218,9 +255,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&bars->o_final, 1);
     // Barriers the softmax warps signal take one arrival per warp after a warp sync (256
     // per-thread arrivals on one barrier are 256 serialised shared-memory atomics).
-    mbar_init(&bars->o_empty, 8);
-    mbar_init(&bars->ep, 8);
-    mbar_init(&bars->staged, 8);
+    mbar_init(&bars->o_empty, 4);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->ml_full[i], 8);
+      mbar_init(&bars->ml_empty[i], 4);
+    }
+    mbar_init(&bars->stage_free, 1);
+    mbar_init(&bars->staged, 4);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars->item_full[i], 1);
       mbar_init(&bars->item_empty[i], kItemConsumers);
@@ -275,7 +316,131 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // Each role branch starts with its warpgroup's setmaxnreg so that the register limit
   // ptxas applies to the code after it is the one of that branch.
-  if (warp >= 8) {
+  if (warp >= kEpilogueWarp0) {
+    regs_dec<kEpilogueRegs>();
+    // ------------------------------------------------------------ epilogue (warps 12-15)
+    // Per item: merge the two halves' accumulators exactly,
+    //   m = max(m_a, m_b), l = l_a 2^(m_a-m) + l_b 2^(m_b-m),
+    //   o = (O_a 2^(m_a-m) + O_b 2^(m_b-m)) / l,
+    // convert, stage in shared memory and write with one TMA store (fp32 partials: direct
+    // stores), while the softmax warps already work on the next item. Thread lane i of warp
+    // w owns query row 32*(w%4) + i (its TMEM lane), all D output columns.
+    const int quarter = warp & 3;
+    const int r_in_tile = quarter * 32 + lane;
+    const uint32_t lane_bits = static_cast<uint32_t>(quarter * 32) << 16;
+    const bool leader = warp == kEpilogueWarp0 && lane == 0;  // issues the TMA stores
+    bool ok = true;
+    for (int ic = 0; ok; ++ic) {
+      Item w;
+      if (!next_item(ic, true, w)) break;
+      const int slot = ic & 1;
+      const int row = w.q_row0 + r_in_tile;
+      if (!OUT_F32) {
+        // The previous item's TMA store must have read the staging buffer.
+        if (leader) {
+          bulk_wait_group_read0();
+          mbar_arrive(&bars->stage_free);
+        }
+        ok = mbar_wait_bounded(&bars->stage_free, ic & 1, abort_flag, kTimeoutNs);
+      }
+      if (ok) ok = mbar_wait_bounded(&bars->ml_full[slot], (ic >> 1) & 1, abort_flag, kTimeoutNs);
+      if (ok) ok = mbar_wait_bounded(&bars->o_final, ic & 1, abort_flag, kTimeoutNs);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      const float* red_i = red + slot * (4 * kRowsPerTile);
+      const float m_a = red_i[r_in_tile], m_b = red_i[kRowsPerTile + r_in_tile];
+      const float l_a = red_i[2 * kRowsPerTile + r_in_tile];
+      const float l_b = red_i[3 * kRowsPerTile + r_in_tile];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->ml_empty[slot]);
+      const float m = fmaxf(m_a, m_b);
+      // A half that saw no valid key has m = -inf: weight 0.
+      const float w_a = m_a == -INFINITY ? 0.f : ex2_approx(m_a - m);
+      const float w_b = m_b == -INFINITY ? 0.f : ex2_approx(m_b - m);
+      const float l_tot = l_a * w_a + l_b * w_b;
+      // Rows without any valid key (only with a key slice) get o = 0 and lse = -inf.
+      const float inv_l = l_tot > 0.f ? 1.f / l_tot : 0.f;
+      const float f_a = w_a * inv_l, f_b = w_b * inv_l;
+      const bool in_range = row < p.S;
+      const uint32_t t_oa = tmem + lane_bits + L::kOCol;
+#pragma unroll 1
+      for (int c = 0; c < D / 16; ++c) {
+        uint32_t oa[16], ob[16];
+        if (w.n_kv > 0) {
+          tmem_ld16(t_oa + c * 16, oa);
+          tmem_ld16(t_oa + D + c * 16, ob);
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) oa[i] = ob[i] = 0u;
+        }
+        float v[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          v[i] = __uint_as_float(oa[i]) * f_a + __uint_as_float(ob[i]) * f_b;
+        if constexpr (OUT_F32) {
+          if (in_range) {
+            float4* dst = reinterpret_cast<float4*>(
+                reinterpret_cast<uint8_t*>(p.o) +
+                4 * (static_cast<int64_t>(w.split) * p.o_split_stride +
+                     static_cast<int64_t>(w.b) * p.o_sb + static_cast<int64_t>(w.h) * p.o_sh +
+                     static_cast<int64_t>(row) * p.o_ss + c * 16));
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              if (c * 16 + 4 * i < p.d_out)  // columns beyond the true head dim
+                dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+          }
+        } else {
+          // 16 output columns = two 16-byte units of the 128-byte-swizzled staging row (the
+          // layout the tensor map's SWIZZLE_128B expects: unit u of row r at
+          // r*128 + ((u ^ (r % 8)) * 16) within its 64-column chunk).
+          const int col = c * 16;
+          uint8_t* chunk = smem + L::kStageOff + (col / 64) * (kRowsPerTile * 128);
+          const int u0 = (col % 64) / 8;
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            const uint4 val = make_uint4(pack2<BF16>(v[8 * i], v[8 * i + 1]),
+                                         pack2<BF16>(v[8 * i + 2], v[8 * i + 3]),
+                                         pack2<BF16>(v[8 * i + 4], v[8 * i + 5]),
+                                         pack2<BF16>(v[8 * i + 6], v[8 * i + 7]));
+            *reinterpret_cast<uint4*>(chunk + r_in_tile * 128 +
+                                      (((u0 + i) ^ (r_in_tile & 7)) * 16)) = val;
+          }
+        }
+      }
+      // O may now be overwritten by the next item's first P.V.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->o_empty);
+      if (!OUT_F32) {
+        // Hand the staged tile to the TMA store (issued by the leader once all 4 warps wrote
+        // their part; rows beyond S are clipped by the tensor map).
+        fence_proxy_async_shared();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->staged);
+        if (leader) {
+          if (mbar_wait_bounded(&bars->staged, ic & 1, abort_flag, kTimeoutNs)) {
+#pragma unroll
+            for (int c = 0; c < L::kChunks; ++c)
+              tma_store_4d(&tmap_o, smem + L::kStageOff + c * (kRowsPerTile * 128), c * 64,
+                           w.q_row0, w.h, w.b);
+            bulk_commit_group();
+          } else {
+            ok = false;
+          }
+        }
+      }
+      if (leader) TRACE_ITEM(ic, 3);
+      if (p.lse != nullptr && in_range)
+        p.lse[static_cast<int64_t>(w.split) * p.BH * p.S + static_cast<int64_t>(w.bh) * p.S + row] =
+            l_tot > 0.f ? (m + __log2f(l_tot)) * 0.69314718055994531f : -INFINITY;
+      ok = __all_sync(0xffffffffu, ok);
+    }
+    // Stores must have completed before the CTA exits.
+    if (!OUT_F32 && leader) bulk_wait_group0();
+    if (!ok && lane == 0 && !*abort_flag) report(p, TA_DEVSTAT_TIMEOUT_EPILOG, abort_flag);
+  } else if (warp >= 8) {
   regs_dec<kSideRegs>();
   if (warp == kProducerWarp) {
     // ------------------------------------------------------------ scheduler + TMA producer
@@ -383,18 +548,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           TRACE(ic, j, 8);
           tc_fence_after();
           const uint64_t vd = v_desc + static_cast<uint64_t>((st * L::kTileBytes) >> 4);
-          // P_g[:, keys 64*hh .. 64*hh+63] . V[those keys] into O_hh.
-#pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            const uint32_t a_tmem = tmem + buf * 128 + hh * kKeysPerHalf;
-            const uint32_t d_tmem = tmem + L::kOCol + hh * D;
-#pragma unroll
-            for (int k4 = 0; k4 < kKeysPerHalf / 16; ++k4) {
-              const int kk = hh * (kKeysPerHalf / 16) + k4;  // 16-key step within the V tile
-              mma_ts(d_tmem, a_tmem + k4 * 8, vd + static_cast<uint64_t>((kk * 16 * 128) >> 4),
-                     kIdescPV, (j > 0 || k4 > 0) ? 1u : 0u);
-            }
-          }
+          // P_g[:, keys 64*hh .. 64*hh+63] . V[those keys] into O_hh (offsets as immediates:
+          // the issuer runs on few registers).
+          const uint32_t acc = j > 0 ? 1u : 0u;
+          pv_half_mmas<0>(tmem + L::kOCol, tmem + buf * 128, vd, kIdescPV, acc);
+          pv_half_mmas<1>(tmem + L::kOCol + D, tmem + buf * 128 + kKeysPerHalf, vd, kIdescPV, acc);
           mma_commit(&bars->pv_done[g & 3]);
           mma_commit(&bars->v_empty[st]);
           ++v_it;
@@ -437,13 +595,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!ok) break;
           tc_fence_after();
           const uint64_t kd = k_desc + static_cast<uint64_t>((st * L::kTileBytes) >> 4);
-          const uint32_t d_tmem = tmem + buf * 128;
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            constexpr int kAtom = kRowsPerTile * 128;
-            const uint64_t off = static_cast<uint64_t>(((kk >> 2) * kAtom + (kk & 3) * 32) >> 4);
-            mma_ss(d_tmem, q_desc + off, kd + off, kIdescQK, kk > 0 ? 1u : 0u);
-          }
+          qk_mmas<D>(tmem + buf * 128, q_desc, kd, kIdescQK);
           mma_commit(&bars->s_full[buf]);
           mma_commit(&bars->k_empty[st]);
           ++k_it;
@@ -621,117 +773,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(&bars->p_full[buf]);
       }
       if (!ok) break;
-      // ---- epilogue of the item: merge the two halves. Exchange (m, l) with the partner
-      // thread (same row, other warpgroup) through the slot of this item's parity, then
-      // each warpgroup writes D/2 output columns from both accumulators.
-      float* red_i = red + (ic & 1) * (4 * kRowsPerTile);
+      // ---- end of the item: hand (m, l) of this half to the epilogue warpgroup through the
+      // slot of the item's parity and go on with the next item at once.
+      const int slot = ic & 1;
+      ok = mbar_wait_bounded(&bars->ml_empty[slot], ((ic >> 1) & 1) ^ 1, abort_flag, kTimeoutNs);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      float* red_i = red + slot * (4 * kRowsPerTile);
       red_i[half * kRowsPerTile + r_in_tile] = m_run;
       red_i[2 * kRowsPerTile + half * kRowsPerTile + r_in_tile] = l_run;
-      // The thread that issues the output TMA store makes sure the previous item's store has
-      // finished reading the staging buffer before anyone passes this exchange.
-      if (!OUT_F32 && threadIdx.x == 0) bulk_wait_group_read0();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->ep);
-      ok = mbar_wait_bounded(&bars->ep, ic & 1, abort_flag, kTimeoutNs);
-      if (ok) ok = mbar_wait_bounded(&bars->o_final, ic & 1, abort_flag, kTimeoutNs);
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok) {
-        if (lane == 0 && !*abort_flag) report(p, TA_DEVSTAT_TIMEOUT_EPILOG, abort_flag);
-        break;
-      }
-      tc_fence_after();
+      if (lane == 0) mbar_arrive(&bars->ml_full[slot]);
       if (threadIdx.x == 0) TRACE_ITEM(ic, 2);
-      const float m_a = red_i[r_in_tile], m_b = red_i[kRowsPerTile + r_in_tile];
-      const float l_a = red_i[2 * kRowsPerTile + r_in_tile];
-      const float l_b = red_i[3 * kRowsPerTile + r_in_tile];
-      const float m = fmaxf(m_a, m_b);
-      // A half that saw no valid key has m = -inf: weight 0.
-      const float w_a = m_a == -INFINITY ? 0.f : ex2_approx(m_a - m);
-      const float w_b = m_b == -INFINITY ? 0.f : ex2_approx(m_b - m);
-      const float l_tot = l_a * w_a + l_b * w_b;
-      // Rows without any valid key (only with a key slice) get o = 0 and lse = -inf.
-      const float inv_l = l_tot > 0.f ? 1.f / l_tot : 0.f;
-      const float f_a = w_a * inv_l, f_b = w_b * inv_l;
-      const bool in_range = row < p.S;
-      const int col0 = half * (D / 2);  // output columns of this warpgroup
-      const uint32_t t_oa = tmem + lane_bits + L::kOCol + col0;
-#pragma unroll 1
-      for (int c = 0; c < D / 64; ++c) {
-        uint32_t oa[32], ob[32];
-        if (w.n_kv > 0) {
-          tmem_ld32(t_oa + c * 32, oa);
-          tmem_ld32(t_oa + D + c * 32, ob);
-          tmem_wait_ld();
-          reg_fence32(oa);
-          reg_fence32(ob);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) oa[i] = ob[i] = 0u;
-        }
-        float* v = reinterpret_cast<float*>(oa);  // merged values, in place
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          v[i] = __uint_as_float(oa[i]) * f_a + __uint_as_float(ob[i]) * f_b;
-        if constexpr (OUT_F32) {
-          if (in_range) {
-            float4* dst = reinterpret_cast<float4*>(
-                reinterpret_cast<uint8_t*>(p.o) +
-                4 * (static_cast<int64_t>(w.split) * p.o_split_stride +
-                     static_cast<int64_t>(w.b) * p.o_sb + static_cast<int64_t>(w.h) * p.o_sh +
-                     static_cast<int64_t>(row) * p.o_ss + col0 + c * 32));
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-              if (col0 + c * 32 + 4 * i < p.d_out)  // columns beyond the true head dim
-                dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-          }
-        } else {
-          // 32 output columns = four 16-byte units of the 128-byte-swizzled staging row
-          // (the layout the tensor map's SWIZZLE_128B expects: unit u of row r at
-          // r*128 + ((u ^ (r % 8)) * 16) within its 64-column chunk).
-          const int col = col0 + c * 32;
-          uint8_t* chunk = smem + L::kStageOff + (col / 64) * (kRowsPerTile * 128);
-          const int u0 = (col % 64) / 8;
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const uint4 val = make_uint4(pack2<BF16>(v[8 * i], v[8 * i + 1]),
-                                         pack2<BF16>(v[8 * i + 2], v[8 * i + 3]),
-                                         pack2<BF16>(v[8 * i + 4], v[8 * i + 5]),
-                                         pack2<BF16>(v[8 * i + 6], v[8 * i + 7]));
-            *reinterpret_cast<uint4*>(chunk + r_in_tile * 128 +
-                                      (((u0 + i) ^ (r_in_tile & 7)) * 16)) = val;
-          }
-        }
-      }
-      // O may now be overwritten by the next item's first P.V.
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->o_empty);
-      if (!OUT_F32) {
-        // Hand the staged tile to the TMA store (issued by thread 0 once all 256 threads
-        // wrote their part; rows beyond S are clipped by the tensor map).
-        fence_proxy_async_shared();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars->staged);
-        if (threadIdx.x == 0) {
-          if (mbar_wait_bounded(&bars->staged, ic & 1, abort_flag, kTimeoutNs)) {
-#pragma unroll
-            for (int c = 0; c < L::kChunks; ++c)
-              tma_store_4d(&tmap_o, smem + L::kStageOff + c * (kRowsPerTile * 128), c * 64,
-                           w.q_row0, w.h, w.b);
-            bulk_commit_group();
-          } else {
-            ok = false;
-          }
-        }
-      }
-      if (threadIdx.x == 0) TRACE_ITEM(ic, 3);
-      if (half == 0 && p.lse != nullptr && in_range)
-        p.lse[static_cast<int64_t>(w.split) * p.BH * p.S + static_cast<int64_t>(w.bh) * p.S + row] =
-            l_tot > 0.f ? (m + __log2f(l_tot)) * 0.69314718055994531f : -INFINITY;
-      ok = __all_sync(0xffffffffu, ok);
     }
-    // Stores must have completed before the CTA exits.
-    if (!OUT_F32 && threadIdx.x == 0) bulk_wait_group0();
     if (!ok && lane == 0 && !*abort_flag) report(p, TA_DEVSTAT_TIMEOUT_SOFTMAX, abort_flag);
   }
 

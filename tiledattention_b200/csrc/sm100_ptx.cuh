@@ -169,6 +169,47 @@ __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_
       : "memory");
 }
 
+// The same two MMAs with the descriptor offsets (16-byte units) and the accumulate flag as
+// immediates: the adds happen inside the asm block, so an unrolled sequence keeps only the
+// base descriptors in registers (a thread issuing MMAs on few registers needs that).
+template <uint32_t kAOff, uint32_t kBOff, uint32_t kAcc>
+__device__ __forceinline__ void mma_ss_imm(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                           uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 a, b;\n\t"
+      "add.s64 a, %1, %4;\n\t"
+      "add.s64 b, %2, %5;\n\t"
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "n"(kAOff), "n"(kBOff), "n"(kAcc)
+      : "memory");
+}
+template <uint32_t kATmemOff, uint32_t kBOff, uint32_t kAcc>
+__device__ __forceinline__ void mma_ts_imm(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                           uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 b;\n\t.reg .b32 a;\n\t"
+      "add.u32 a, %1, %4;\n\t"
+      "add.s64 b, %2, %5;\n\t"
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "n"(kATmemOff), "n"(kBOff), "n"(kAcc)
+      : "memory");
+}
+// Same as mma_ts_imm with the accumulate flag given at run time.
+template <uint32_t kATmemOff, uint32_t kBOff>
+__device__ __forceinline__ void mma_ts_imm_acc(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                               uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 b;\n\t.reg .b32 a;\n\t"
+      "add.u32 a, %1, %5;\n\t"
+      "add.s64 b, %2, %6;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(acc), "n"(kATmemOff), "n"(kBOff)
+      : "memory");
+}
+
 // Arrive once on `bar` when every tcgen05 async op issued so far by this thread is done.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile(
@@ -196,6 +237,17 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
         "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
         "=r"(r[31])
+      : "r"(taddr));
+}
+
+// Each thread of the warp reads 16 consecutive 32-bit columns of its own TMEM lane.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
 }
 
