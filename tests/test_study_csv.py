@@ -37,3 +37,20 @@ def test_error_rows_and_csv_roundtrip(tmp_path):
     back = list(csv.DictReader(open(path)))
     assert back[0]["status"] == "ok" and back[1]["status"] == "error"
     assert float(back[0]["flops_forward"]) == 2 * 8 * 4096 * 4097 * 128
+
+
+def test_settle_option_reaches_the_sweep(tmp_path, monkeypatch):
+    seen = {}
+
+    def fake_sweep(*args, **kwargs):
+        seen.update(kwargs)
+        return []
+
+    monkeypatch.setattr(study, "run_sweep", fake_sweep)
+    out = tmp_path / "s.csv"
+    study.main(["--out", str(out), "--settle-s", "0.5", "--seq", "512"])
+    assert seen["settle_s"] == 0.5
+    assert out.read_text().startswith(REFERENCE_HEADER)
+    seen.clear()
+    study.main(["--out", str(out), "--seq", "512"])
+    assert seen["settle_s"] == 0.0  # default: the reference harness's timing

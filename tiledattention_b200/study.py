@@ -25,6 +25,7 @@ import argparse
 import csv
 import math
 import statistics
+import time
 
 COLUMNS = [
     "method", "baseline_name", "dtype", "causal", "B", "H", "S", "D", "flops_forward",
@@ -95,7 +96,10 @@ def time_cuda_callable(torch, fn, warmup: int, iters: int, flush=None) -> tuple[
 
 
 def run_sweep(seqs, dims, dtypes, causals, methods, warmup=5, iters=15, b=1, h=8, seed=1234,
-              flush_l2=False):
+              flush_l2=False, settle_s=0.0):
+    """`settle_s` > 0: leave the GPU idle that long before timing each (shape, method), so a
+    method timed right after a seconds-long heavy shape does not run in the SM-clock dip that
+    follows such a load under the power cap (an option beyond the reference's timing)."""
     import torch
     from torch.nn.attention import SDPBackend, sdpa_kernel
 
@@ -136,6 +140,9 @@ def run_sweep(seqs, dims, dtypes, causals, methods, warmup=5, iters=15, b=1, h=8
                     q, k, v = (torch.randn(b, h, s, d, device=dev, dtype=dtype) for _ in range(3))
                     for method in methods:
                         fn = impls[method]
+                        if settle_s > 0:
+                            torch.cuda.synchronize()
+                            time.sleep(settle_s)
                         try:
                             med, tail = time_cuda_callable(torch, lambda: fn(q, k, v, causal),
                                                            warmup, iters, flush)
@@ -168,13 +175,15 @@ def main(argv=None) -> None:
     ap.add_argument("--heads", type=int, nargs="+", default=[8])
     ap.add_argument("--flush-l2", action="store_true",
                     help="rewrite a 256 MB buffer before every timed call (cold L2)")
+    ap.add_argument("--settle-s", type=float, default=0.0,
+                    help="idle seconds before timing each (shape, method); 0 as the reference")
     args = ap.parse_args(argv)
     rows = []
     for b in args.batch:
         for h in args.heads:
             rows += run_sweep(args.seq, args.dims, args.dtypes, [c == "True" for c in args.causal],
                               args.methods, args.warmup, args.iters, b=b, h=h,
-                              flush_l2=args.flush_l2)
+                              flush_l2=args.flush_l2, settle_s=args.settle_s)
     write_csv(rows, args.out)
     print(f"wrote {len(rows)} rows to {args.out}")
 
