@@ -120,6 +120,19 @@ __host__ __device__ constexpr int poly_every() {
 #endif
 }
 
+// Suspend-time hint (ns) of the kernel's barrier waits (0: none). With it, the warps that wait
+// for most of an item (epilogue, producer, issuers) poll less and leave more issue slots to
+// the softmax warps on their sub-partitions. Measured on B200 (100 us): +3.7 % at D=64
+// non-causal, +0.4 % causal; -0.5 % at D=128, where it stays off.
+template <int D>
+__host__ __device__ constexpr uint32_t wait_hint_ns() {
+#ifdef TA_WAIT_HINT_NS_D64
+  return D == 64 ? TA_WAIT_HINT_NS_D64 : 0u;
+#else
+  return D == 64 ? 100000u : 0u;
+#endif
+}
+
 template <int D>
 struct Layout {
   static_assert(D == 64 || D == 128, "this kernel serves head dims 64 and 128");
@@ -231,6 +244,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   using L = Layout<D>;
   constexpr int NB = L::kSBufs;
   constexpr int kPolyEvery = poly_every<D>();
+  constexpr uint32_t kWaitHint = wait_hint_ns<D>();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -299,7 +313,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // threads themselves, the softmax warps through lane 0.
   auto next_item = [&](int ic, bool warp_release, Item& w) -> bool {
     const int slot = ic & 1;
-    bool got = mbar_wait_bounded(&bars->item_full[slot], (ic >> 1) & 1, abort_flag, kTimeoutNs);
+    bool got = mbar_wait_bounded<kWaitHint>(&bars->item_full[slot], (ic >> 1) & 1, abort_flag, kTimeoutNs);
     if (warp_release) got = __all_sync(0xffffffffu, got);
     if (got) {
       const int* v = bars->item[slot];
@@ -341,10 +355,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           bulk_wait_group_read0();
           mbar_arrive(&bars->stage_free);
         }
-        ok = mbar_wait_bounded(&bars->stage_free, ic & 1, abort_flag, kTimeoutNs);
+        ok = mbar_wait_bounded<kWaitHint>(&bars->stage_free, ic & 1, abort_flag, kTimeoutNs);
       }
-      if (ok) ok = mbar_wait_bounded(&bars->ml_full[slot], (ic >> 1) & 1, abort_flag, kTimeoutNs);
-      if (ok) ok = mbar_wait_bounded(&bars->o_final, ic & 1, abort_flag, kTimeoutNs);
+      if (ok) ok = mbar_wait_bounded<kWaitHint>(&bars->ml_full[slot], (ic >> 1) & 1, abort_flag, kTimeoutNs);
+      if (ok) ok = mbar_wait_bounded<kWaitHint>(&bars->o_final, ic & 1, abort_flag, kTimeoutNs);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
@@ -420,7 +434,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars->staged);
         if (leader) {
-          if (mbar_wait_bounded(&bars->staged, ic & 1, abort_flag, kTimeoutNs)) {
+          if (mbar_wait_bounded<kWaitHint>(&bars->staged, ic & 1, abort_flag, kTimeoutNs)) {
 #pragma unroll
             for (int c = 0; c < L::kChunks; ++c)
               tma_store_4d(&tmap_o, smem + L::kStageOff + c * (kRowsPerTile * 128), c * 64,
@@ -454,7 +468,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t ph = (it / n_st) & 1;
         uint64_t* empty = is_v ? &bars->v_empty[st] : &bars->k_empty[st];
         uint64_t* full = is_v ? &bars->v_full[st] : &bars->k_full[st];
-        if (!mbar_wait_bounded(empty, ph ^ 1, abort_flag, kTimeoutNs)) {
+        if (!mbar_wait_bounded<kWaitHint>(empty, ph ^ 1, abort_flag, kTimeoutNs)) {
           if (!*abort_flag) report(p, TA_DEVSTAT_TIMEOUT_LOAD, abort_flag);
           ok = false;
           return;
@@ -469,7 +483,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (; ok; ++ic) {
         // Publish the next item (or kNoItem) once its slot was released.
         const int slot = ic & 1;
-        if (!mbar_wait_bounded(&bars->item_empty[slot], ((ic >> 1) & 1) ^ 1, abort_flag,
+        if (!mbar_wait_bounded<kWaitHint>(&bars->item_empty[slot], ((ic >> 1) & 1) ^ 1, abort_flag,
                                kTimeoutNs)) {
           if (!*abort_flag) report(p, TA_DEVSTAT_TIMEOUT_LOAD, abort_flag);
           break;
@@ -486,7 +500,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive(&bars->item_full[slot]);
         if (w.split < 0) break;
         // Q: the previous item's QK^T MMAs must be done with the buffer.
-        if (!mbar_wait_bounded(&bars->q_empty, (ic & 1) ^ 1, abort_flag, kTimeoutNs)) {
+        if (!mbar_wait_bounded<kWaitHint>(&bars->q_empty, (ic & 1) ^ 1, abort_flag, kTimeoutNs)) {
           if (!*abort_flag) report(p, TA_DEVSTAT_TIMEOUT_LOAD, abort_flag);
           break;
         }
@@ -506,12 +520,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       volatile int no_abort = 0;
       bool drained = true;
       if (ic > 0)
-        drained &= mbar_wait_bounded(&bars->q_full, (ic - 1) & 1, &no_abort, kTimeoutNs);
+        drained &= mbar_wait_bounded<kWaitHint>(&bars->q_full, (ic - 1) & 1, &no_abort, kTimeoutNs);
       for (int i = max(0, k_it - L::kKStages); i < k_it; ++i)
-        drained &= mbar_wait_bounded(&bars->k_full[i % L::kKStages], (i / L::kKStages) & 1,
+        drained &= mbar_wait_bounded<kWaitHint>(&bars->k_full[i % L::kKStages], (i / L::kKStages) & 1,
                                      &no_abort, kTimeoutNs);
       for (int i = max(0, v_it - L::kVStages); i < v_it; ++i)
-        drained &= mbar_wait_bounded(&bars->v_full[i % L::kVStages], (i / L::kVStages) & 1,
+        drained &= mbar_wait_bounded<kWaitHint>(&bars->v_full[i % L::kVStages], (i / L::kVStages) & 1,
                                      &no_abort, kTimeoutNs);
       if (!drained && p.status) atomicOr(p.status, TA_DEVSTAT_TIMEOUT_DRAIN);
     }
@@ -524,7 +538,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       // Self-test of the failure path: wait on a barrier nothing arrives on, so the wait
       // runs out, the kernel records the timeout and every role returns.
-      if (p.selftest_stall) ok = mbar_wait_bounded(&bars->never, 0, abort_flag, kTimeoutNs);
+      if (p.selftest_stall) ok = mbar_wait_bounded<kWaitHint>(&bars->never, 0, abort_flag, kTimeoutNs);
       int g = 0, v_it = 0;
       for (int ic = 0; ok; ++ic) {
         Item w;
@@ -532,18 +546,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         // The previous item's epilogue must have read O before PV_0 overwrites it (and
         // before o_final of this item, so o_final never completes twice unobserved).
         if (ic > 0) {
-          ok = mbar_wait_bounded(&bars->o_empty, (ic - 1) & 1, abort_flag, kTimeoutNs);
+          ok = mbar_wait_bounded<kWaitHint>(&bars->o_empty, (ic - 1) & 1, abort_flag, kTimeoutNs);
           if (!ok) break;
         }
         for (int j = 0; ok && j < w.n_kv; ++j, ++g) {
           const int buf = g % NB;
           const int st = v_it % L::kVStages;
-          ok = mbar_wait_bounded(&bars->v_full[st], (v_it / L::kVStages) & 1, abort_flag,
+          ok = mbar_wait_bounded<kWaitHint>(&bars->v_full[st], (v_it / L::kVStages) & 1, abort_flag,
                                  kTimeoutNs);
           if (!ok) break;
           // One barrier per buffer: a warpgroup may run up to NB-1 tiles ahead of the
           // other, never NB (S_{g+NB} needs PV_g), so no phase completes unobserved.
-          ok = mbar_wait_bounded(&bars->p_full[buf], (g / NB) & 1, abort_flag, kTimeoutNs);
+          ok = mbar_wait_bounded<kWaitHint>(&bars->p_full[buf], (g / NB) & 1, abort_flag, kTimeoutNs);
           if (!ok) break;
           TRACE(ic, j, 8);
           tc_fence_after();
@@ -578,19 +592,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int ic = 0; ok; ++ic) {
         Item w;
         if (!next_item(ic, false, w)) break;
-        ok = mbar_wait_bounded(&bars->q_full, ic & 1, abort_flag, kTimeoutNs);
+        ok = mbar_wait_bounded<kWaitHint>(&bars->q_full, ic & 1, abort_flag, kTimeoutNs);
         for (int t = 0; ok && t < w.n_kv; ++t, ++g) {
           const int buf = g % NB;
           // S_g overwrites P_{g-NB}: wait until PV_{g-NB} completed. Barrier (g-NB)%4
           // completes next for PV_{g-NB+4}, which needs S_{g-NB+4} (not issued yet), so
           // the phase test is unambiguous.
           if (g >= NB) {
-            ok = mbar_wait_bounded(&bars->pv_done[(g - NB) & 3], ((g - NB) >> 2) & 1,
+            ok = mbar_wait_bounded<kWaitHint>(&bars->pv_done[(g - NB) & 3], ((g - NB) >> 2) & 1,
                                    abort_flag, kTimeoutNs);
             if (!ok) break;
           }
           const int st = k_it % L::kKStages;
-          ok = mbar_wait_bounded(&bars->k_full[st], (k_it / L::kKStages) & 1, abort_flag,
+          ok = mbar_wait_bounded<kWaitHint>(&bars->k_full[st], (k_it / L::kKStages) & 1, abort_flag,
                                  kTimeoutNs);
           if (!ok) break;
           tc_fence_after();
@@ -613,7 +627,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Drain: all MMAs of both issuers complete before tensor memory is freed.
   if (warp == kPvWarp && lane == 0) {
     volatile int no_abort = 0;
-    if (!mbar_wait_bounded(&bars->drain, 0, &no_abort, kTimeoutNs) && p.status)
+    if (!mbar_wait_bounded<kWaitHint>(&bars->drain, 0, &no_abort, kTimeoutNs) && p.status)
       atomicOr(p.status, TA_DEVSTAT_TIMEOUT_DRAIN);
   }
   __syncwarp();
@@ -641,7 +655,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; j < w.n_kv; ++j, ++g) {
         const int buf = g % NB;
         const uint32_t t_s = tmem + lane_bits + buf * 128;
-        ok = mbar_wait_bounded(&bars->s_full[buf], (g / NB) & 1, abort_flag, kTimeoutNs);
+        ok = mbar_wait_bounded<kWaitHint>(&bars->s_full[buf], (g / NB) & 1, abort_flag, kTimeoutNs);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
@@ -740,7 +754,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           // for PV_{g-1}. Barrier (g-1)%4 completes next for PV_{g+3}, which needs this
           // warpgroup's P_{g+3}; PV_{g-5} completed before S_g could be issued (S_g waits
           // for PV_{g-NB}, NB <= 3). So the phase test is unambiguous.
-          bool done = mbar_wait_bounded(&bars->pv_done[(g - 1) & 3], ((g - 1) >> 2) & 1,
+          bool done = mbar_wait_bounded<kWaitHint>(&bars->pv_done[(g - 1) & 3], ((g - 1) >> 2) & 1,
                                         abort_flag, kTimeoutNs);
           done = __all_sync(0xffffffffu, done);
           if (!done) {
@@ -776,7 +790,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---- end of the item: hand (m, l) of this half to the epilogue warpgroup through the
       // slot of the item's parity and go on with the next item at once.
       const int slot = ic & 1;
-      ok = mbar_wait_bounded(&bars->ml_empty[slot], ((ic >> 1) & 1) ^ 1, abort_flag, kTimeoutNs);
+      ok = mbar_wait_bounded<kWaitHint>(&bars->ml_empty[slot], ((ic >> 1) & 1) ^ 1, abort_flag, kTimeoutNs);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       float* red_i = red + slot * (4 * kRowsPerTile);

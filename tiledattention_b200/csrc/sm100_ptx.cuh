@@ -52,30 +52,46 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
 // try_wait may suspend the thread in hardware until the phase completes or a
 // system-dependent time limit elapses, which keeps waiting warps from spending issue slots
 // on polling.
+// kHintNs > 0: the suspend-time hint of try_wait. The thread then stays suspended until the
+// phase completes or about kHintNs have passed, so a warp that waits long polls less often.
+template <uint32_t kHintNs = 0>
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity) {
   uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar_addr), "r"(parity)
-      : "memory");
+  if constexpr (kHintNs > 0) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar_addr), "r"(parity), "n"(kHintNs)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar_addr), "r"(parity)
+        : "memory");
+  }
   return ok != 0;
 }
 
 // Wait until the phase with the given parity of `bar` has completed, or give up.
 // Gives up when `abort_flag` (shared) becomes non-zero or after `timeout_ns` of
-// global time; returns false in both cases. Never spins unbounded.
+// global time; returns false in both cases. Never spins unbounded. With a suspend-time hint
+// the flag and the clock are checked every 4th try (at most ~4 hints apart).
+template <uint32_t kHintNs = 0>
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
                                                   volatile int* abort_flag,
                                                   uint64_t timeout_ns) {
   const uint32_t a = smem_u32(bar);
-  if (mbar_try_wait(a, parity)) return true;
+  if (mbar_try_wait<kHintNs>(a, parity)) return true;
   const uint64_t t0 = global_timer_ns();
+  constexpr uint32_t kCheckMask = kHintNs > 0 ? 3u : 63u;
   for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait(a, parity)) return true;
-    if ((it & 63u) == 0u) {
+    if (mbar_try_wait<kHintNs>(a, parity)) return true;
+    if ((it & kCheckMask) == 0u) {
       if (*abort_flag) return false;
       if (global_timer_ns() - t0 > timeout_ns) return false;
     }
