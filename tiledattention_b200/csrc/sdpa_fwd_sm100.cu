@@ -110,13 +110,15 @@ constexpr int kItemConsumers = 2 + 8 + 4;
 constexpr int kNoItem = -1;  // Item::split of "no item left"
 
 // Every kPolyEvery-th element pair computes exp2 on the FMA pipe instead of the MUFU
-// (0: never). Worth it only where the MUFU is the limit and the MMA work is small (D=64).
-template <int D>
+// (0: never). Worth it only where the MUFU is the limit and the MMA work is small (D=64):
+// measured on B200, every 3rd pair is fastest without a mask, every 5th with the causal mask
+// (whose diagonal tiles add FMA-pipe masking work); at D=128 it does not pay.
+template <int D, bool CAUSAL>
 __host__ __device__ constexpr int poly_every() {
 #if defined(TA_POLY_EVERY_D64) && defined(TA_POLY_EVERY_D128)
   return D == 64 ? TA_POLY_EVERY_D64 : TA_POLY_EVERY_D128;
 #else
-  return D == 64 ? 4 : 0;
+  return D == 64 ? (CAUSAL ? 5 : 3) : 0;
 #endif
 }
 
@@ -243,7 +245,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const __grid_constant__ CUtensorMap tmap_o, const FwdParams p) {
   using L = Layout<D>;
   constexpr int NB = L::kSBufs;
-  constexpr int kPolyEvery = poly_every<D>();
+  constexpr int kPolyEvery = poly_every<D, CAUSAL>();
   constexpr uint32_t kWaitHint = wait_hint_ns<D>();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
